@@ -1,0 +1,421 @@
+"""Benchmark of the tiered paged-decode hot path (BASELINE metric: paged-decode tok/s and
+local+peer GB/s as % of roofline).
+
+Default workload (one B200, all-local): a full 36-layer
+Qwen3-8B-shaped KV pool of 1,048,576 token slots per plane (72 planes x 2 KiB
+x (C+1) slots = 154.6 GB in HBM), batch 64, KV lengths uniform in [2048, 32768]
+(seeded; redrawn with the next seed while the sum exceeds the pool), slots a
+seeded random permutation of the pool, Q/K/V ~ N(0, 1) bf16.  One step = the
+packer (unified read order for the batch) + 36 layers of tiered decode
+(decode kernel + merge).  Per-layer KV (4.5 GB) is far larger than L2, so no
+flush is needed between iterations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dual|reference] [--workload config2|small]
+
+Under torchrun (N > 1) every rank serves its own independent batch (decode
+shards by request; no collective on the data path): scaling "weak".
+``--impl reference`` times the reference's CPU attention math (the fp32 oracle
+restatement of check_attention_output) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "paged-decode tok/s and local+peer GB/s as % roofline at 1/2/4/8 B200"
+UNIT = "tok/s"
+FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    # name: (batch, Lmin, Lmax, pool slots C, layers)
+    "config2": (64, 2048, 32768, 1 << 20, 36),
+    "small": (16, 2048, 32768, 1 << 18, 4),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["dual", "reference"], default="dual")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="config2")
+    ap.add_argument("--seed", type=int, default=20261101)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def draw_lengths(batch, lmin, lmax, capacity, seed):
+    """Seeded U[lmin, lmax] lengths; redraw with seed+1, ... while the sum exceeds the pool."""
+    for k in range(1000):
+        rng = np.random.default_rng(seed + k)
+        L = rng.integers(lmin, lmax + 1, batch)
+        if L.sum() <= capacity:
+            return L.astype(np.int64), seed + k
+    raise RuntimeError("could not draw lengths that fit the pool")
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle sampling during the timed region (exact PID, no patterns)."""
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.gpu = gpu_index
+
+    def start(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- dual arm
+class DecodeWorkload:
+    def __init__(self, args, device):
+        from dual_b200 import ops
+        self.ops = ops
+        B, lmin, lmax, C, layers = WORKLOADS[args.workload]
+        self.B, self.C, self.layers, self.device = B, C, layers, device
+        self.lengths, self.seed_used = draw_lengths(B, lmin, lmax, C, args.seed)
+        self.T = int(self.lengths.sum())
+        g = torch.Generator(device=device).manual_seed(args.seed)
+        # 36 layers x (K, V) planes, page 0 is SGLang's dummy slot
+        self.k = [torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=device) for _ in range(layers)]
+        self.v = [torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=device) for _ in range(layers)]
+        for t in self.k + self.v:
+            t.normal_(generator=g)
+        perm = (torch.randperm(C, generator=g, device=device) + 1).to(torch.int32)
+        maxL = int(self.lengths.max())
+        self.tier = torch.full((B, maxL), -1, dtype=torch.int32, device=device)
+        self.slot = torch.zeros((B, maxL), dtype=torch.int32, device=device)
+        off = 0
+        for b, L in enumerate(self.lengths.tolist()):
+            self.tier[b, :L] = 0
+            self.slot[b, :L] = perm[off:off + L]
+            off += L
+        self.req = torch.arange(B, dtype=torch.int32, device=device)
+        self.seq = torch.tensor(self.lengths, dtype=torch.int32, device=device)
+        self.indptr = torch.tensor(np.concatenate([[0], np.cumsum(self.lengths)]), dtype=torch.int32, device=device)
+        self.indices = torch.empty(self.T, dtype=torch.int32, device=device)
+        self.q = torch.randn((layers, B, 32, 128), generator=g, device=device).to(torch.bfloat16)
+        self.out = torch.empty((layers, B, 32, 128), dtype=torch.bfloat16, device=device)
+        self.lse = torch.empty((layers, B, 32), dtype=torch.float32, device=device)
+        self.num_ctas = ops.default_ctas(device.index)
+        self.ws = torch.zeros(ops.decode_workspace_size(B, self.num_ctas), dtype=torch.uint8, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.scale = 128 ** -0.5
+
+    def step(self, events=None):
+        ops = self.ops
+        ops.pack_read_order(self.tier, self.slot, self.req, self.seq, self.C, 5, 32, self.indices, status=self.status)
+        for i in range(self.layers):
+            if events is not None:
+                events[i][0].record()
+            ops.tiered_decode(self.q[i], self.k[i], self.v[i], self.C, [], [], self.indptr, self.indices, self.scale,
+                              self.out[i], self.lse[i], self.ws, self.num_ctas)
+            if events is not None:
+                events[i][1].record()
+
+    def bytes_per_layer(self):
+        return 4096 * self.T + 8192 * self.B * 2 + 128 * self.B
+
+    def launches_per_step(self):
+        return 1 + 2 * self.layers
+
+
+class E2E:
+    """Same metric through the public wrapper API with host buffers: per step H2D of the step's
+    queries (pinned), plan(), the packer, 36 x wrapper.run, D2H of the outputs (pinned)."""
+
+    def __init__(self, w: DecodeWorkload):
+        from dual_b200.wrapper import BatchDecodeWithPagedKVCacheWrapper
+        self.w = w
+        self.q_host = torch.randn(w.q.shape, dtype=torch.float32).to(torch.bfloat16).pin_memory()
+        self.out_host = torch.empty(w.out.shape, dtype=torch.bfloat16).pin_memory()
+        self.indptr_host = w.indptr.cpu().pin_memory()
+        self.q_dev = torch.empty_like(w.q)
+        self.wrapper = BatchDecodeWithPagedKVCacheWrapper(torch.empty(64 << 20, dtype=torch.uint8, device=w.device),
+                                                          "NHD", use_tensor_cores=True)
+        self.last = torch.ones(w.B, dtype=torch.int32)
+
+    def step(self):
+        w = self.w
+        self.q_dev.copy_(self.q_host, non_blocking=True)
+        w.ops.pack_read_order(w.tier, w.slot, w.req, w.seq, w.C, 5, 32, w.indices, status=w.status)
+        self.wrapper.plan(self.indptr_host, w.indices, self.last, 32, 8, 128, 1, q_data_type=torch.bfloat16,
+                          sm_scale=w.scale)
+        for i in range(w.layers):
+            self.wrapper.run(self.q_dev[i], (w.k[i], w.v[i]), out=w.out[i])
+        self.out_host.copy_(w.out, non_blocking=True)
+
+    def h2d_bytes(self):
+        return self.q_host.numel() * 2 + self.indptr_host.numel() * 4
+
+    def d2h_bytes(self):
+        return self.out_host.numel() * 2
+
+
+def cpu_baseline(w: DecodeWorkload, budget_s=12.0):
+    """Reference fp32 attention math (oracle restatement) on the host cores, bounded sample:
+    a few of this batch's requests for one layer, repeated until ~budget_s; scaled to tok/s."""
+    from oracle.attention import attend
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    order = np.argsort(w.lengths)
+    picks = [int(order[len(order) // 2]), int(order[len(order) // 4]), int(order[3 * len(order) // 4])]
+    data = []
+    for b in picks:
+        L = int(w.lengths[b])
+        s = w.slot[b, :L].long()
+        data.append((w.q[0, b:b + 1].cpu(), w.k[0].index_select(0, s).cpu(), w.v[0].index_select(0, s).cpu(), L))
+    tokens, t0 = 0, time.perf_counter()
+    reps = 0
+    while True:
+        for q, k, v, L in data:
+            attend(q, k, v, L - 1, w.scale)
+            tokens += L
+        reps += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    per_token_layer = dt / tokens                       # seconds per KV token per layer
+    step_s = per_token_layer * w.T * w.layers           # whole batch, all layers
+    return {"value": w.B / step_s, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(picks)} of {w.B} requests (L={[d[3] for d in data]}), layer 0, x{reps} reps; "
+                      f"scaled by sum(L)={w.T} and {w.layers} layers"}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_dual(args):
+    world, rank, local = dist_setup(args)
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    w = DecodeWorkload(args, device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(args.warmup, 3)):
+        w.step()
+    torch.cuda.synchronize()
+    status = int(w.status.item()) | int(w.ws[:4].view(torch.int32).item())
+    # timed region
+    events = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(w.layers)]
+    layer_ms = []
+    clocks = ClockSampler(device.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    all_events = []
+    for _ in range(args.steps):
+        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(w.layers)]
+        w.step(ev)
+        all_events.append(ev)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    for ev in all_events:
+        layer_ms += [a.elapsed_time(b) for a, b in ev]
+    ms_max = max_over_ranks(ms, world, device)
+    tok = w.B * args.steps * world
+    value = tok / (ms_max / 1e3)
+    layer_avg = sum(layer_ms) / len(layer_ms)
+    peak, peak_kind = measured_peaks()
+    achieved = w.bytes_per_layer() / (layer_avg / 1e3) / 1e9
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: 1xB200 all-local tiered paged decode, {w.layers} layers",
+                   "batch_per_gpu": w.B, "kv_len": f"U[{WORKLOADS[args.workload][1]},{WORKLOADS[args.workload][2]}]",
+                   "sum_kv_tokens": w.T, "length_seed": w.seed_used, "pool_slots": w.C, "layers": w.layers,
+                   "heads": "32q/8kv x 128", "page_size": 1, "parallelism": f"replicas x{world} (request-sharded)",
+                   "l2": f"inputs larger than L2 ({w.bytes_per_layer() / 1e9:.2f} GB per layer)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(w),
+                     "peak_source": f"{peak_kind} hbm_gbs", "kernel": "tiered_decode_kernel + decode_merge_kernel",
+                     "layer_ms": round(layer_avg, 4), "algorithmic_bytes_per_launch": w.bytes_per_layer()},
+        "gpu_launches": w.launches_per_step() * args.steps,
+        "device_status": status,
+    }
+    if clk:
+        result["clocks"] = clk
+    if not args.no_e2e:
+        result["e2e"] = run_e2e(w, args, world, device)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(w)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def traffic_per_launch(w):
+    """DRAM bytes per decode launch from the committed ncu summary (bytes per KV token, scaled)."""
+    p = ROOT / "profiles" / "decode_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return int(d["dram_bytes_per_kv_token"] * w.T + d.get("dram_bytes_per_request", 0) * w.B)
+
+
+def run_e2e(w, args, world, device):
+    e = E2E(w)
+    for _ in range(3):
+        e.step()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        e.step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b), world, device)
+    return {"value": round(w.B * args.steps * world / (ms / 1e3), 2), "unit": UNIT,
+            "h2d_bytes_per_step": e.h2d_bytes(), "d2h_bytes_per_step": e.d2h_bytes(),
+            "api": "dual_b200.wrapper.BatchDecodeWithPagedKVCacheWrapper.plan/run (C ABI) + packer"}
+
+
+# -------------------------------------------------------------- reference arm
+def run_reference(args):
+    """The reference's CPU attention math (fp32 torch restatement of check_attention_output,
+    oracle port) on this host's cores, same workload definition; bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.attention import attend
+    B, lmin, lmax, C, layers = WORKLOADS[args.workload]
+    lengths, seed_used = draw_lengths(B, lmin, lmax, C, args.seed)
+    T = int(lengths.sum())
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(args.seed)
+    order = np.argsort(lengths)
+    b = int(order[len(order) // 2])
+    L = int(lengths[b])
+    # sample: one request of the batch, one layer, gathered from a scattered pool of 4L slots
+    pool_k = torch.randn((4 * L, 8, 128), generator=g).to(torch.bfloat16)
+    pool_v = torch.randn((4 * L, 8, 128), generator=g).to(torch.bfloat16)
+    slots = torch.randperm(4 * L, generator=g)[:L]
+    q = torch.randn((1, 32, 128), generator=g).to(torch.bfloat16)
+
+    def one():
+        attend(q, pool_k.index_select(0, slots), pool_v.index_select(0, slots), L - 1, 128 ** -0.5)
+
+    for _ in range(max(args.warmup, 1)):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    dt = (time.perf_counter() - t0) / args.steps
+    step_s = dt / L * T * layers
+    value = B / step_s
+    sample = f"1 of {B} requests (L={L}), 1 layer per step; scaled by sum(L)={T} and {layers} layers"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: CPU fp32 reference attention math", "batch": B,
+                   "sum_kv_tokens": T, "length_seed": seed_used, "layers": layers},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_dual(args)
+
+
+if __name__ == "__main__":
+    main()

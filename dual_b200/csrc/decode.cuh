@@ -1,0 +1,96 @@
+// Tiered split-KV paged GQA decode for sm_100a.
+//
+// Replaces the FlashInfer FA2 batch-prefill JIT module that the reference
+// patches with `paged_kv_t::tiered_address` and uses for decode
+// (final/cooperative_4gpu/code/peer/flashinfer_peer.py:27-78 resolver,
+// :105-142 module, hook peer/backend.py:132-138).  Page ids follow the same
+// encoding: p <= C is local slot p; p > C is global remote id g = p - C - 1,
+// held by supplier bank g % num_peers at physical slot g / num_peers
+// (peer/flashinfer_peer.py:44-54, peer/remote_bank.py:1,21).
+//
+// Design (B200-first, page_size 1):
+//   * One CTA owns a contiguous range of the flattened token axis
+//     [g*T/G, (g+1)*T/G) for one head group of HG kv heads.  The range may span
+//     several requests; each request-segment is flushed as one partial state.
+//   * A producer warp resolves each page id once and issues ONE
+//     cp.async.bulk per token row and plane (HG*256 B, contiguous in the NHD
+//     pool), local HBM and peer HBM alike (no multicast), into an NS-deep
+//     shared-memory ring completed by mbarrier transaction counts.  The deep
+//     ring keeps ~180 rows in flight per SM, which hides NVLink latency for the
+//     remote rows without stalling the local stream.
+//   * HG*NPH consumer warps: warp (h, ph) computes kv head h on every NPH-th
+//     tile with bf16 m16n8k16 tensor-core MMAs (the 4 query heads of the GQA
+//     group are the MMA rows) and an exp2-domain online softmax.
+//   * Partial (O, m, d) states go to the workspace; a merge kernel combines
+//     them per (request, q head) with a log-sum-exp reduction and writes the
+//     bf16 output and the base-2 LSE (FlashInfer's convention).
+#pragma once
+#include "common.cuh"
+
+namespace dual {
+
+constexpr int kHeadDim = 128;
+constexpr int kNumQoHeads = 32;
+constexpr int kNumKvHeads = 8;
+constexpr int kGqa = kNumQoHeads / kNumKvHeads;  // 4 query heads per kv head
+constexpr int kMaxPeers = 8;
+constexpr int kPartialStride = 132;  // floats per (segment, q head): O[128], m, d, pad
+
+struct TieredDecodeParams {
+  const __nv_bfloat16* q;  // [B, 32, 128]
+  int64_t q_stride_tok, q_stride_head;  // elements
+  const char* k_local;     // local pool, page p at k_local + p * local_stride (bytes)
+  const char* v_local;
+  int64_t local_stride;    // bytes per slot (heads contiguous, 256 B each)
+  int64_t local_capacity;  // C: valid local pages are 0..C
+  const char* peer_k[kMaxPeers];
+  const char* peer_v[kMaxPeers];
+  int num_peers;
+  int64_t peer_stride;     // bytes per slot in every supplier bank
+  int64_t peer_slots;      // physical slots per supplier bank
+  const int32_t* indptr;   // [B+1]
+  const int32_t* indices;  // unified page ids, indptr[B] entries
+  int64_t num_indices;     // capacity of `indices` (reads never go beyond it)
+  int batch;
+  float scale_log2;        // sm_scale * log2(e)
+  float* partial;          // workspace
+  unsigned* status;        // workspace status word
+  int grid_g;              // CTAs per head group
+  __nv_bfloat16* out;      // [B, 32, 128]
+  int64_t out_stride_tok, out_stride_head;
+  float* lse;              // [B, 32] (base 2) or nullptr
+};
+
+template <int HG_, int NS_, int TILE_, int NPH_>
+struct DecodeConfig {
+  static constexpr int HG = HG_;        // kv heads per CTA
+  static constexpr int NS = NS_;        // ring stages
+  static constexpr int TILE = TILE_;    // token rows per stage
+  static constexpr int NPH = NPH_;      // consumer phases (tiles interleaved across warps)
+  static constexpr int NHG = kNumKvHeads / HG;
+  static constexpr int ROW_BYTES = HG * kHeadDim * 2;
+  static constexpr int PITCH = ROW_BYTES + 16;  // +16 B: conflict-free ldmatrix rows
+  static constexpr int PLANE_BYTES = TILE * PITCH;
+  static constexpr int STAGE_BYTES = 2 * PLANE_BYTES;
+  static constexpr int CONSUMERS = HG * NPH;
+  static constexpr int THREADS = (CONSUMERS + 1) * 32;
+  static constexpr int RED_FLOATS = NPH * HG * kGqa * kPartialStride;
+  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + RED_FLOATS * 4 + 2 * NS * 8 + 16;
+  static constexpr int ROWS = HG * kGqa;  // q heads per CTA
+  static_assert(TILE == 16, "consumer MMA tiling assumes 16 token rows per stage");
+  static_assert(kNumKvHeads % HG == 0, "head groups must tile the kv heads");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+using DecodeCfg = DecodeConfig<2, 11, 16, 4>;
+
+// Workspace layout: [status: 256 B][partials].
+inline size_t decode_workspace_bytes(int batch, int grid_g) {
+  return 256 + sizeof(float) * size_t(DecodeCfg::NHG) * size_t(grid_g + batch) * DecodeCfg::ROWS *
+                   kPartialStride;
+}
+
+cudaError_t launch_tiered_decode(const TieredDecodeParams& p, cudaStream_t stream);
+int decode_default_grid_g(int device);
+
+}  // namespace dual

@@ -1,0 +1,174 @@
+"""Torch-tensor front end of the C-ABI kernels (device pointers + current stream).
+
+PyTorch only supplies device memory and streams here; every computation is a
+kernel from libdual_b200.so.  Functions validate shapes/dtypes on the host and
+launch asynchronously on ``torch.cuda.current_stream()``; all of them are safe
+inside CUDA-graph capture (no host synchronisation, no allocation) except
+``status`` which reads the device status word back.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+
+NUM_QO_HEADS = 32
+NUM_KV_HEADS = 8
+HEAD_DIM = 128
+SLOT_BYTES = NUM_KV_HEADS * HEAD_DIM * 2  # one token slot of one plane (K or V) of one layer
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _dev(t: torch.Tensor) -> int:
+    if t.device.type != "cuda":
+        raise ValueError(f"expected a CUDA tensor, got {t.device}")
+    return t.device.index
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def decode_workspace_size(batch: int, num_ctas: int = 0) -> int:
+    return int(_lib.load().dual_decode_workspace_size(int(batch), int(num_ctas)))
+
+
+def default_ctas(device: int = 0) -> int:
+    return int(_lib.load().dual_decode_default_ctas(int(device)))
+
+
+def _pool_stride(pool: torch.Tensor, name: str) -> int:
+    """Byte stride between consecutive token slots of an NHD page_size-1 plane."""
+    _check(pool.dtype == torch.bfloat16, f"{name} must be bf16")
+    if pool.dim() == 4:  # [pages, page_size=1, heads, dim]
+        _check(pool.shape[1] == 1, f"{name}: page_size must be 1")
+        _check(pool.stride(3) == 1 and pool.stride(2) == HEAD_DIM, f"{name}: heads x dim must be contiguous")
+        _check(tuple(pool.shape[2:]) == (NUM_KV_HEADS, HEAD_DIM), f"{name}: expected 8 kv heads x 128")
+    else:
+        _check(pool.dim() == 3 and tuple(pool.shape[1:]) == (NUM_KV_HEADS, HEAD_DIM),
+               f"{name}: expected [slots, 8, 128] or [slots, 1, 8, 128]")
+        _check(pool.stride(2) == 1 and pool.stride(1) == HEAD_DIM, f"{name}: heads x dim must be contiguous")
+    return pool.stride(0) * 2
+
+
+def tiered_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor, local_capacity: int,
+                  peer_k: Sequence[torch.Tensor], peer_v: Sequence[torch.Tensor],
+                  kv_indptr: torch.Tensor, unified_indices: torch.Tensor, sm_scale: float,
+                  out: torch.Tensor, lse: Optional[torch.Tensor], workspace: torch.Tensor,
+                  num_ctas: int = 0, batch: Optional[int] = None) -> None:
+    """One decode layer over the tiered pool (local HBM + supplier banks)."""
+    dev = _dev(q)
+    B = q.shape[0] if batch is None else int(batch)
+    _check(q.dtype == torch.bfloat16 and q.dim() == 3 and tuple(q.shape[1:]) == (NUM_QO_HEADS, HEAD_DIM)
+           and q.stride(2) == 1, "q must be bf16 [B, 32, 128] with contiguous head_dim")
+    _check(out.dtype == torch.bfloat16 and out.dim() == 3 and out.stride(2) == 1, "out must be bf16 [B, 32, 128]")
+    _check(kv_indptr.dtype == torch.int32 and unified_indices.dtype == torch.int32, "indptr/indices must be int32")
+    _check(kv_indptr.numel() >= B + 1, "kv_indptr too short")
+    if lse is not None:
+        _check(lse.dtype == torch.float32 and lse.is_contiguous() and lse.numel() >= B * NUM_QO_HEADS,
+               "lse must be contiguous fp32 [B, 32]")
+    ls = _pool_stride(k_local, "k_local")
+    _check(_pool_stride(v_local, "v_local") == ls, "k/v local pools must share a slot stride")
+    n = len(peer_k)
+    _check(len(peer_v) == n, "peer_k / peer_v count mismatch")
+    pk = (C.c_void_p * max(n, 1))(*[p.data_ptr() for p in peer_k])
+    pv = (C.c_void_p * max(n, 1))(*[p.data_ptr() for p in peer_v])
+    ps, slots = 0, 0
+    if n:
+        ps = _pool_stride(peer_k[0], "peer_k0")
+        slots = peer_k[0].shape[0]
+        for i in range(n):
+            _check(_pool_stride(peer_k[i], f"peer_k{i}") == ps and _pool_stride(peer_v[i], f"peer_v{i}") == ps,
+                   "all supplier banks must share a slot stride")
+            _check(peer_k[i].shape[0] == slots and peer_v[i].shape[0] == slots, "supplier banks differ in size")
+    lib = _lib.load()
+    _lib.check(lib.dual_tiered_decode(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_local.data_ptr(), v_local.data_ptr(), ls, int(local_capacity),
+        pk, pv, n, ps, slots,
+        kv_indptr.data_ptr(), unified_indices.data_ptr(), unified_indices.numel(), B,
+        float(sm_scale),
+        out.data_ptr(), out.stride(0), out.stride(1), _ptr(lse),
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(), int(num_ctas),
+        dev, _stream(q.device)))
+
+
+def pack_read_order(tier: torch.Tensor, slot: torch.Tensor, req_pool_indices: torch.Tensor,
+                    seq_lens: torch.Tensor, local_capacity: int, remote_rows: int, tile_rows: int,
+                    full_out: torch.Tensor, prefix_lens: Optional[torch.Tensor] = None,
+                    history_out: Optional[torch.Tensor] = None, new_loc: Optional[torch.Tensor] = None,
+                    status: Optional[torch.Tensor] = None) -> None:
+    """Unified index list in the interleaved read order (decode: prefix_lens=None)."""
+    dev = _dev(tier)
+    for name, t in (("tier", tier), ("slot", slot), ("req_pool_indices", req_pool_indices),
+                    ("seq_lens", seq_lens), ("full_out", full_out)):
+        _check(t.dtype == torch.int32, f"{name} must be int32")
+    _check(tier.shape == slot.shape and tier.stride() == slot.stride() and tier.stride(1) == 1,
+           "tier/slot must be row-major tables of one shape")
+    if prefix_lens is not None:
+        _check(prefix_lens.dtype == torch.int32, "prefix_lens must be int32")
+    if new_loc is not None:
+        _check(new_loc.dtype == torch.int64, "new_loc must be int64 (out_cache_loc)")
+    B = req_pool_indices.numel()
+    lib = _lib.load()
+    _lib.check(lib.dual_pack_read_order(
+        tier.data_ptr(), slot.data_ptr(), tier.shape[0], tier.stride(0), req_pool_indices.data_ptr(), seq_lens.data_ptr(),
+        _ptr(prefix_lens), _ptr(new_loc), B, int(local_capacity), int(remote_rows), int(tile_rows),
+        full_out.data_ptr(), _ptr(history_out), _ptr(status), dev, _stream(tier.device)))
+
+
+def write_prefill_layout(tier: torch.Tensor, slot: torch.Tensor, req_pool_indices: torch.Tensor,
+                         start: torch.Tensor, length: torch.Tensor, prefix: torch.Tensor,
+                         locations: torch.Tensor, max_length: int, status: Optional[torch.Tensor] = None) -> None:
+    """tier=0, slot=locations for the newly appended positions of every request."""
+    dev = _dev(tier)
+    _check(locations.dtype in (torch.int64, torch.int32), "locations must be int32 or int64")
+    for name, t in (("req", req_pool_indices), ("start", start), ("length", length), ("prefix", prefix)):
+        _check(t.dtype == torch.int32, f"{name} must be int32")
+    lib = _lib.load()
+    _lib.check(lib.dual_write_prefill_layout(
+        tier.data_ptr(), slot.data_ptr(), tier.shape[0], tier.stride(0), req_pool_indices.data_ptr(),
+        start.data_ptr(), length.data_ptr(), prefix.data_ptr(), locations.data_ptr(),
+        int(locations.dtype == torch.int64), req_pool_indices.numel(), int(max_length), _ptr(status), dev,
+        _stream(tier.device)))
+
+
+def migrate_copy(local_planes: torch.Tensor, remote_planes: torch.Tensor, num_planes: int, num_banks: int,
+                 source: torch.Tensor, target: torch.Tensor, reverse: bool, local_slots: int,
+                 remote_slots: int, status: torch.Tensor, row_bytes: int = SLOT_BYTES, max_ctas: int = 0) -> None:
+    """Byte-exact copy of token slots across all planes between the local pool and supplier banks."""
+    dev = _dev(source)
+    _check(local_planes.dtype == torch.int64 and remote_planes.dtype == torch.int64, "pointer tables must be int64")
+    _check(local_planes.numel() >= num_planes and remote_planes.numel() >= num_banks * num_planes,
+           "pointer tables too short")
+    _check(source.dtype == torch.int64 and target.dtype == torch.int64 and source.numel() == target.numel(),
+           "source/target must be int64 of equal length")
+    _check(status.dtype in (torch.int32, torch.uint32) and status.numel() >= 1, "status must be a 32-bit word")
+    lib = _lib.load()
+    _lib.check(lib.dual_migrate_copy(
+        local_planes.data_ptr(), remote_planes.data_ptr(), int(num_planes), int(num_banks), source.data_ptr(),
+        target.data_ptr(), source.numel(), int(bool(reverse)), int(row_bytes), int(local_slots), int(remote_slots),
+        status.data_ptr(), int(max_ctas), dev, _stream(source.device)))
+
+
+def status_clear(status: torch.Tensor) -> None:
+    lib = _lib.load()
+    _lib.check(lib.dual_status_clear(status.data_ptr(), _dev(status), _stream(status.device)))
+
+
+def status_read(status: torch.Tensor) -> int:
+    lib = _lib.load()
+    v = C.c_uint32(0)
+    _lib.check(lib.dual_status_read(status.data_ptr(), C.byref(v), _dev(status), _stream(status.device)))
+    return int(v.value)

@@ -1,0 +1,149 @@
+/*
+ * dual_b200 C ABI -- the drop-in boundary of the tiered-KV hot path.
+ *
+ * Plain pointers and sizes only; every call is asynchronous on the given CUDA
+ * stream (a cudaStream_t passed as void*, NULL = legacy default stream) and is
+ * safe to capture in a CUDA graph unless stated otherwise.  Every function
+ * returns 0 on success or a nonzero DUAL_E* code, in which case
+ * dual_last_error() returns a thread-local message.  Device-side problems
+ * (bad page ids, timed-out waits) are recorded as bits in a caller-provided
+ * 32-bit device status word (see DUAL_STATUS_*), never as traps.
+ *
+ * Model constants fixed by the reference (Qwen3-8B layer, page_size 1):
+ * 32 query heads, 8 kv heads, head_dim 128, bf16 KV, NHD layout.
+ */
+#ifndef DUAL_B200_H
+#define DUAL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ error codes */
+#define DUAL_OK 0
+#define DUAL_EINVAL 1     /* bad argument (shape, null pointer, alignment) */
+#define DUAL_ECUDA 2      /* a CUDA runtime call failed */
+#define DUAL_ENOSPACE 3   /* workspace too small */
+#define DUAL_EUNSUPPORTED 4
+
+/* device status bits (written by kernels into the caller's status word) */
+#define DUAL_STATUS_BAD_LOCAL_SLOT 0x1u
+#define DUAL_STATUS_BAD_REMOTE_SLOT 0x2u
+#define DUAL_STATUS_WAIT_TIMEOUT 0x4u
+#define DUAL_STATUS_BAD_COPY_SLOT 0x8u
+#define DUAL_STATUS_BAD_LENGTH 0x10u
+#define DUAL_STATUS_BAD_TIER 0x20u
+
+/* Thread-local message of the last failing call ("" if none). */
+const char* dual_last_error(void);
+/* ABI version of this library (major * 100 + minor). */
+int dual_abi_version(void);
+
+/* ------------------------------------------------------- tiered decode ---
+ * Replaces the patched FlashInfer FA2 batch-prefill module used for decode:
+ *   peer/flashinfer_peer.py:27-78   paged_kv_t::tiered_address (page-id resolver)
+ *   peer/flashinfer_peer.py:105-142 module(): custom JIT with extra tensors
+ *     peer_k0..peer_v2, unified_indices and scalars local_capacity, sm_scale
+ *   peer/backend.py:132-138         wrapper.run(q, paged_kv, *peers, indices, C, scale)
+ * Page id p in unified_indices: p <= local_capacity -> local slot p;
+ * else g = p - local_capacity - 1 -> peer bank g % num_peers, slot g / num_peers.
+ *
+ * q           [batch, 32, 128] bf16, strides in elements (q_stride_head even)
+ * k_local/v_local  local pool planes of one layer, slot p at base + p*local_stride_bytes,
+ *             8 heads x 128 bf16 contiguous per slot (NHD, page_size 1)
+ * peer_k/peer_v    host arrays of num_peers (0..8) device pointers (may be peer
+ *             GPUs' memory mapped by IPC or peer access), same per-slot layout
+ * kv_indptr   [batch+1] int32 device prefix sums of kv lengths
+ * unified_indices  kv_indptr[batch] int32 page ids in read order; num_indices is the
+ *             buffer's capacity (entries beyond it are never read: the status word
+ *             records DUAL_STATUS_BAD_LENGTH and the tail is skipped)
+ * out         [batch, 32, 128] bf16; lse [batch, 32] fp32 (base 2, FlashInfer's
+ *             convention) or NULL
+ * workspace   device scratch of >= dual_decode_workspace_size(batch, num_ctas)
+ *             bytes; its first 4 bytes are the status word (cleared by
+ *             dual_status_clear, never by this call)
+ * num_ctas    CTAs per head group (0 = one wave: SMs / 4); fixed per graph capture
+ */
+size_t dual_decode_workspace_size(int batch, int num_ctas);
+int dual_decode_default_ctas(int device);
+int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                       const void* k_local, const void* v_local, int64_t local_stride_bytes,
+                       int64_t local_capacity,
+                       const void* const* peer_k, const void* const* peer_v, int num_peers,
+                       int64_t peer_stride_bytes, int64_t peer_slots,
+                       const int32_t* kv_indptr, const int32_t* unified_indices, int64_t num_indices,
+                       int batch, double sm_scale,
+                       void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                       void* workspace, size_t workspace_bytes, int num_ctas,
+                       int device, void* stream);
+
+/* ------------------------------------------------------ read-order packer ---
+ * Replaces Triton _count_remote/_pack_indices + Engine.prepare (peer/backend.py:22-79)
+ * and packing.prepare (peer/packing.py:6-36); exact order = peer/layout.py:5-22.
+ * tier/slot   [table_rows, table_stride] int32 tables (tier 0 local / 1 remote / -1 unused);
+ *             rows/positions outside them are skipped and flagged in status
+ * prefix_lens NULL for decode (prefix = seq_lens) or [batch] for prefill/append
+ * new_loc     NULL or [batch] int64: fused decode-step write of the newest token
+ *             (slot[req, seq-1] = new_loc, tier = 0) before packing
+ * full_out    sum(seq_lens) int32; history_out NULL or sum(prefix_lens) int32
+ * status      NULL or a device status word
+ */
+int dual_pack_read_order(int32_t* tier, int32_t* slot, int64_t table_rows, int64_t table_stride,
+                         const int32_t* req_pool_indices, const int32_t* seq_lens,
+                         const int32_t* prefix_lens, const int64_t* new_loc, int batch,
+                         int64_t local_capacity, int remote_rows, int tile_rows,
+                         int32_t* full_out, int32_t* history_out, uint32_t* status,
+                         int device, void* stream);
+
+/* Replaces Triton _write_prefill_layout (peer/page_ops.py:6-18): for every request b and
+ * j < length[b]: slot[req[b], prefix[b]+j] = locations[start[b]+j], tier[...] = 0.
+ * locations are int64 (SGLang out_cache_loc) when loc_is_int64, else int32.  Writes outside the
+ * [table_rows, table_stride] tables are skipped (status, when given, records DUAL_STATUS_BAD_LENGTH). */
+int dual_write_prefill_layout(int32_t* tier, int32_t* slot, int64_t table_rows, int64_t table_stride,
+                              const int32_t* req_pool_indices, const int32_t* start,
+                              const int32_t* length, const int32_t* prefix,
+                              const void* locations, int loc_is_int64, int batch, int max_length,
+                              uint32_t* status, int device, void* stream);
+
+/* ------------------------------------------------------------- migration ---
+ * Replaces Triton fused_copy._copy / copy_pages / restore (peer/fused_copy.py:6-33):
+ * for each i < n and each plane: reverse==0 copies local slot source[i] to remote id
+ * target[i] (bank target[i] % num_banks, slot target[i] / num_banks); reverse==1 copies
+ * remote id source[i] to local slot target[i].  Bit-exact byte copy.
+ * local_planes [num_planes] and remote_planes [num_banks*num_planes] are DEVICE int64
+ * arrays of plane base pointers (RemoteBank.pointers layout, peer/remote_bank.py:23).
+ * max_ctas bounds the SMs the copy occupies (0 = as many as rows need). */
+int dual_migrate_copy(const int64_t* local_planes, const int64_t* remote_planes, int num_planes,
+                      int num_banks, const int64_t* source, const int64_t* target, int64_t n,
+                      int reverse, int64_t row_bytes, int64_t local_slots, int64_t remote_slots,
+                      uint32_t* status, int max_ctas, int device, void* stream);
+
+/* --------------------------------------------------------------- status --- */
+int dual_status_clear(uint32_t* status, int device, void* stream);
+/* Synchronous read of a device status word (not capturable). */
+int dual_status_read(const uint32_t* status, uint32_t* value_out, int device, void* stream);
+
+/* ------------------------------------------------- peer memory / topology ---
+ * Replace the ctypes CUDA-IPC helper V/nvlink_cooperation/cuda_ipc.py:18-88
+ * (Cuda.allocate/open/close/free/enable_peer/attributes) and the NVLink checks of
+ * peer/host4.py:27-62.  Handles are the 64-byte cudaIpcMemHandle_t payload. */
+int dual_supplier_alloc(int device, size_t bytes, void** ptr_out, unsigned char handle_out[64]);
+int dual_supplier_free(int device, void* ptr);
+int dual_ipc_open(int device, const unsigned char handle[64], void** ptr_out);
+int dual_ipc_close(int device, void* ptr);
+int dual_enable_peer(int device, int peer);
+int dual_can_access_peer(int device, int peer, int* out);
+/* attr: 0 performance rank, 1 access supported, 2 native atomics (cudaDevP2PAttr*) */
+int dual_p2p_attribute(int src, int dst, int attr, int* value);
+/* memory_type: cudaMemoryType of ptr; owner_device: its device */
+int dual_pointer_info(const void* ptr, int* memory_type, int* owner_device);
+int dual_device_count(int* count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DUAL_B200_H */

@@ -1,0 +1,60 @@
+"""The C-ABI library loads, exports every symbol include/dual_b200.h declares, and rejects bad
+arguments with error codes + messages.  CPU only: no call here reaches a CUDA API."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from dual_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "dual_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(dual_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 19
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} missing from the ctypes signature table"
+    assert set(_lib.SIGNATURES) == set(names)
+    assert lib.dual_abi_version() == 100
+
+
+def test_argument_errors_are_codes_not_crashes():
+    lib = _lib.load()
+    rc = lib.dual_tiered_decode(None, 0, 0, None, None, 0, 0, None, None, 0, 0, 0, None, None, 0, -1, 0.1,
+                                None, 0, 0, None, None, 0, 0, -1, None)
+    assert rc == 1 and b"batch" in lib.dual_last_error()
+    rc = lib.dual_tiered_decode(None, 0, 0, None, None, 0, 0, None, None, 0, 0, 0, None, None, 0, 4, 0.1,
+                                None, 0, 0, None, None, 0, 0, -1, None)
+    assert rc == 1 and b"null" in lib.dual_last_error()
+    rc = lib.dual_pack_read_order(1, 1, 4, 8, 1, 1, None, None, 2, 100, 32, 32, 1, None, None, -1, None)
+    assert rc == 1 and b"remote_rows" in lib.dual_last_error()
+    rc = lib.dual_migrate_copy(None, None, 72, 3, None, None, -5, 0, 2048, 10, 10, None, 0, -1, None)
+    assert rc == 1
+    rc = lib.dual_migrate_copy(1, 1, 72, 3, 1, 1, 4, 0, 2047, 10, 10, 1, 0, -1, None)
+    assert rc == 1 and b"row_bytes" in lib.dual_last_error()
+    with pytest.raises(_lib.DualError):
+        _lib.check(lib.dual_write_prefill_layout(None, None, 1, 1, None, None, None, None, None, 1, 3, 5, None, -1, None))
+
+
+def test_workspace_size_formula():
+    lib = _lib.load()
+    # 256 B header + 4 head groups x (G + B) segments x 8 q heads x 132 floats
+    assert lib.dual_decode_workspace_size(64, 37) == 256 + 4 * (37 + 64) * 8 * 132 * 4
+    assert lib.dual_decode_workspace_size(1, 1) == 256 + 4 * 2 * 8 * 132 * 4
+
+
+def test_no_cpu_fallback(monkeypatch, tmp_path):
+    """The product path fails loudly when the CUDA library is missing."""
+    monkeypatch.setattr(_lib, "_LIB", None)
+    monkeypatch.setattr(_lib, "library_path", lambda: tmp_path / "missing.so")
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _lib.load()
