@@ -53,7 +53,7 @@ int dual_abi_version(void) { return 100; }
 
 size_t dual_decode_workspace_size(int batch, int num_ctas) {
   if (batch < 0) batch = 0;
-  if (num_ctas <= 0) num_ctas = 148 / dual::DecodeCfg::NHG;
+  if (num_ctas <= 0) num_ctas = 148;
   return dual::decode_workspace_bytes(batch, num_ctas);
 }
 

@@ -9,18 +9,17 @@
 // (peer/flashinfer_peer.py:44-54, peer/remote_bank.py:1,21).
 //
 // Design (B200-first, page_size 1):
-//   * One CTA owns a contiguous range of the flattened token axis
-//     [g*T/G, (g+1)*T/G) for one head group of HG kv heads.  The range may span
-//     several requests; each request-segment is flushed as one partial state.
-//   * A producer warp resolves each page id once and issues ONE
-//     cp.async.bulk per token row and plane (HG*256 B, contiguous in the NHD
+//   * One CTA (one per SM) owns a contiguous range of the flattened token
+//     axis [g*T/G, (g+1)*T/G) for all 8 kv heads.  The range may span several
+//     requests; each request-segment is flushed as one partial state.
+//   * A producer warp stages the range's page ids into shared memory with
+//     cp.async well ahead of use, resolves each page id once, and issues ONE
+//     cp.async.bulk per token row and plane (2 KiB, contiguous in the NHD
 //     pool), local HBM and peer HBM alike (no multicast), into an NS-deep
-//     shared-memory ring completed by mbarrier transaction counts.  The deep
-//     ring keeps ~180 rows in flight per SM, which hides NVLink latency for the
-//     remote rows without stalling the local stream.
-//   * HG*NPH consumer warps: warp (h, ph) computes kv head h on every NPH-th
-//     tile with bf16 m16n8k16 tensor-core MMAs (the 4 query heads of the GQA
-//     group are the MMA rows) and an exp2-domain online softmax.
+//     shared-memory ring completed by mbarrier transaction counts.
+//   * 8 consumer warps, one per kv head, compute every tile with bf16
+//     m16n8k16 tensor-core MMAs (the 4 query heads of the GQA group are the
+//     MMA rows) and an exp2-domain online softmax.
 //   * Partial (O, m, d) states go to the workspace; a merge kernel combines
 //     them per (request, q head) with a log-sum-exp reduction and writes the
 //     bf16 output and the base-2 LSE (FlashInfer's convention).
@@ -61,33 +60,32 @@ struct TieredDecodeParams {
   float* lse;              // [B, 32] (base 2) or nullptr
 };
 
-template <int HG_, int NS_, int TILE_, int NPH_>
+// One CTA = all 8 kv heads of a token range, so every token row of a plane is
+// one contiguous 2 KiB block moved by ONE bulk copy (the TMA engine sustains
+// HBM rate only for copies of ~2 KiB; 512 B copies cap near 3 TB/s).
+template <int NS_, int TILE_>
 struct DecodeConfig {
-  static constexpr int HG = HG_;        // kv heads per CTA
   static constexpr int NS = NS_;        // ring stages
   static constexpr int TILE = TILE_;    // token rows per stage
-  static constexpr int NPH = NPH_;      // consumer phases (tiles interleaved across warps)
-  static constexpr int NHG = kNumKvHeads / HG;
-  static constexpr int ROW_BYTES = HG * kHeadDim * 2;
-  static constexpr int PITCH = ROW_BYTES + 16;  // +16 B: conflict-free ldmatrix rows
+  static constexpr int ROW_BYTES = kNumKvHeads * kHeadDim * 2;  // 2048 B per token per plane
+  static constexpr int PITCH = ROW_BYTES + 16;                  // +16 B: conflict-free ldmatrix rows
   static constexpr int PLANE_BYTES = TILE * PITCH;
   static constexpr int STAGE_BYTES = 2 * PLANE_BYTES;
-  static constexpr int CONSUMERS = HG * NPH;
+  static constexpr int CONSUMERS = kNumKvHeads;                 // one warp per kv head
   static constexpr int THREADS = (CONSUMERS + 1) * 32;
-  static constexpr int RED_FLOATS = NPH * HG * kGqa * kPartialStride;
-  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + RED_FLOATS * 4 + 2 * NS * 8 + 16;
-  static constexpr int ROWS = HG * kGqa;  // q heads per CTA
+  static constexpr int IDX_CHUNK = 512;                         // page ids staged per chunk
+  static constexpr int IDX_BUFS = 3;
+  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + IDX_BUFS * IDX_CHUNK * 4 + (2 * NS + IDX_BUFS) * 8 + 16;
+  static constexpr int ROWS = kNumQoHeads;                      // q heads per CTA
   static_assert(TILE == 16, "consumer MMA tiling assumes 16 token rows per stage");
-  static_assert(kNumKvHeads % HG == 0, "head groups must tile the kv heads");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-using DecodeCfg = DecodeConfig<2, 11, 16, 4>;
+using DecodeCfg = DecodeConfig<3, 16>;
 
-// Workspace layout: [status: 256 B][partials].
+// Workspace layout: [status: 256 B][partials: (G + B) segments x 32 q heads x 132 floats].
 inline size_t decode_workspace_bytes(int batch, int grid_g) {
-  return 256 + sizeof(float) * size_t(DecodeCfg::NHG) * size_t(grid_g + batch) * DecodeCfg::ROWS *
-                   kPartialStride;
+  return 256 + sizeof(float) * size_t(grid_g + batch) * DecodeCfg::ROWS * kPartialStride;
 }
 
 cudaError_t launch_tiered_decode(const TieredDecodeParams& p, cudaStream_t stream);

@@ -65,7 +65,7 @@ int dual_abi_version(void);
  * workspace   device scratch of >= dual_decode_workspace_size(batch, num_ctas)
  *             bytes; its first 4 bytes are the status word (cleared by
  *             dual_status_clear, never by this call)
- * num_ctas    CTAs per head group (0 = one wave: SMs / 4); fixed per graph capture
+ * num_ctas    CTAs (0 = one per SM); fixed per graph capture
  */
 size_t dual_decode_workspace_size(int batch, int num_ctas);
 int dual_decode_default_ctas(int device);

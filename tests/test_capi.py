@@ -47,9 +47,9 @@ def test_argument_errors_are_codes_not_crashes():
 
 def test_workspace_size_formula():
     lib = _lib.load()
-    # 256 B header + 4 head groups x (G + B) segments x 8 q heads x 132 floats
-    assert lib.dual_decode_workspace_size(64, 37) == 256 + 4 * (37 + 64) * 8 * 132 * 4
-    assert lib.dual_decode_workspace_size(1, 1) == 256 + 4 * 2 * 8 * 132 * 4
+    # 256 B header + (G + B) segments x 32 q heads x 132 floats
+    assert lib.dual_decode_workspace_size(64, 148) == 256 + (148 + 64) * 32 * 132 * 4
+    assert lib.dual_decode_workspace_size(1, 1) == 256 + 2 * 32 * 132 * 4
 
 
 def test_no_cpu_fallback(monkeypatch, tmp_path):
