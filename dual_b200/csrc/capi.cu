@@ -46,6 +46,11 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 }  // namespace
 
+namespace dual {
+// Lets other translation units of this library report through dual_last_error().
+void set_last_error_message(const char* message) { g_last_error = message ? message : ""; }
+}  // namespace dual
+
 extern "C" {
 
 const char* dual_last_error(void) { return g_last_error.c_str(); }

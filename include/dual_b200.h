@@ -80,6 +80,29 @@ int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_h
                        void* workspace, size_t workspace_bytes, int num_ctas,
                        int device, void* stream);
 
+/* Allocation-free variant of dual_tiered_decode.  It has no counterpart in the reference:
+ * it exists for callers that cannot allocate device memory or pass a workspace (a serving
+ * process whose memory manager already owns almost all of HBM and forbids out-of-band
+ * cudaMalloc, or a foreign-language binding that only holds the attention tensors).
+ * The split-KV partial states live in a fixed 8 MiB file-scope device array that every
+ * GPU loading this library holds until exit; (num_ctas + batch) * 16896 + 256 bytes must
+ * fit in it (e.g. batch <= 348 with the default 148 CTAs), otherwise DUAL_ENOSPACE.
+ * All calls on a device share that array and it keeps the last call's contents: calls
+ * that overlap on the GPU race on it.  The first call on a device looks up the array's
+ * address (with that device current); make it before any stream capture.
+ * status: NULL (this call clears the array's own status word and records into it) or a
+ * caller-owned device status word that kernels OR bits into.  Other arguments as for
+ * dual_tiered_decode. */
+int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                               const void* k_local, const void* v_local, int64_t local_stride_bytes,
+                               int64_t local_capacity,
+                               const void* const* peer_k, const void* const* peer_v, int num_peers,
+                               int64_t peer_stride_bytes, int64_t peer_slots,
+                               const int32_t* kv_indptr, const int32_t* unified_indices,
+                               int64_t num_indices, int batch, double sm_scale,
+                               void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                               uint32_t* status, int num_ctas, int device, void* stream);
+
 /* ------------------------------------------------------ read-order packer ---
  * Replaces Triton _count_remote/_pack_indices + Engine.prepare (peer/backend.py:22-79)
  * and packing.prepare (peer/packing.py:6-36); exact order = peer/layout.py:5-22.
