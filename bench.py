@@ -38,10 +38,17 @@ UNIT = "tok/s"
 FALLBACK_HBM_GBS = 6650.0
 
 WORKLOADS = {
-    # name: (batch, Lmin, Lmax, pool slots C, layers)
+    # name: (batch, Lmin, Lmax, pool slots C, layers resident)
     "config2": (64, 2048, 32768, 1 << 20, 36),
     "small": (16, 2048, 32768, 1 << 18, 4),
 }
+# Tiered multi-GPU workloads (one process, compute GPU 0 + supplier GPU 1 reached by peer access):
+# name: (batch, Lmin, Lmax, remote/local ratio, remote placement, RN, TN, layers resident, migrate)
+TIERED = {
+    "config3": (128, 2048, 32768, 0.0599, "tail", 8, 128, 6, False),
+    "config5": (128, 4096, 32768, 0.1797, "prefix", 5, 32, 6, True),
+}
+PEER_GBS = 770.0  # measured peer copy per direction on this pool (NVLink 5, NVSwitch)
 
 
 def parse():
@@ -50,7 +57,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["dual", "reference"], default="dual")
-    ap.add_argument("--workload", choices=list(WORKLOADS), default="config2")
+    ap.add_argument("--workload", choices=list(WORKLOADS) + list(TIERED), default="config2")
     ap.add_argument("--seed", type=int, default=20261101)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -363,6 +370,214 @@ def run_e2e(w, args, world, device):
             "api": "dual_b200.wrapper.BatchDecodeWithPagedKVCacheWrapper.plan/run (C ABI) + packer"}
 
 
+
+# ------------------------------------------------------------ tiered (2 GPUs)
+class TieredWorkload:
+    """Compute GPU 0 reads its local pool from HBM and its remote rows from a supplier bank in
+    GPU 1's HBM (peer access); per-layer pools of `layers` resident layers (a 36-layer pool of this
+    batch does not fit one GPU), the per-step figure is 36 x the per-layer time."""
+
+    def __init__(self, args):
+        from dual_b200 import ops, topology
+        from dual_b200.remote_bank import RemoteBank, local_plane_pointers
+        self.ops = ops
+        B, lmin, lmax, rl, placement, RN, TN, layers, migrate = TIERED[args.workload]
+        self.B, self.layers, self.RN, self.TN, self.migrate = B, layers, RN, TN, migrate
+        self.d0, self.d1 = torch.device("cuda:0"), torch.device("cuda:1")
+        topology.enable_peer(0, 1)
+        rng = np.random.default_rng(args.seed)
+        self.lengths = rng.integers(lmin, lmax + 1, B).astype(np.int64)
+        self.remote = np.rint(self.lengths * rl / (1.0 + rl)).astype(np.int64)
+        self.local = self.lengths - self.remote
+        self.T, self.R = int(self.lengths.sum()), int(self.remote.sum())
+        self.mig_tokens = 2048 if migrate else 0
+        n_bg = 4 * self.mig_tokens  # background (not decoded) positions that migrate each step
+        C = int(self.local.sum()) + n_bg
+        R_cap = self.R + n_bg
+        self.C, self.R_cap = C, R_cap
+        g = torch.Generator(device=self.d0).manual_seed(args.seed)
+        self.k = [torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=self.d0) for _ in range(layers)]
+        self.v = [torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=self.d0) for _ in range(layers)]
+        for t in self.k + self.v:
+            t.normal_(generator=g)
+        bank_t = torch.empty((layers, 2, R_cap, 8, 128), dtype=torch.bfloat16, device=self.d1)
+        bank_t.normal_(generator=torch.Generator(device=self.d1).manual_seed(args.seed + 1))
+        self.bank = RemoteBank([bank_t], layers=layers)
+        perm = (torch.randperm(C, generator=g, device=self.d0) + 1).to(torch.int32)
+        maxL = max(int(self.lengths.max()), n_bg)
+        self.tier = torch.full((B + 1, maxL), -1, dtype=torch.int32, device=self.d0)
+        self.slot = torch.zeros_like(self.tier)
+        off, roff = 0, 0
+        for b in range(B):
+            L, r = int(self.lengths[b]), int(self.remote[b])
+            far = np.zeros(L, bool)
+            if placement == "tail":
+                far[L - r:] = True
+            else:
+                far[:r] = True
+            t = torch.from_numpy(far.astype(np.int32)).to(self.d0)
+            s_ = torch.empty(L, dtype=torch.int32, device=self.d0)
+            fidx = torch.from_numpy(np.nonzero(far)[0]).to(self.d0)
+            nidx = torch.from_numpy(np.nonzero(~far)[0]).to(self.d0)
+            s_[fidx] = torch.arange(roff, roff + r, dtype=torch.int32, device=self.d0)
+            s_[nidx] = perm[off:off + L - r]
+            off += L - r
+            roff += r
+            self.tier[b, :L] = t
+            self.slot[b, :L] = s_
+        # background positions (row B): local slots perm[off:off+n_bg], migrating into ids R .. R_cap-1
+        self.bg_local = perm[off:off + n_bg].long()
+        self.bg_remote = torch.arange(self.R, R_cap, dtype=torch.int64, device=self.d0)
+        self.req = torch.arange(B, dtype=torch.int32, device=self.d0)
+        self.seq = torch.tensor(self.lengths, dtype=torch.int32, device=self.d0)
+        self.indptr = torch.tensor(np.concatenate([[0], np.cumsum(self.lengths)]), dtype=torch.int32, device=self.d0)
+        self.indices = torch.empty(self.T, dtype=torch.int32, device=self.d0)
+        self.q = torch.randn((layers, B, 32, 128), generator=g, device=self.d0).to(torch.bfloat16)
+        self.out = torch.empty_like(self.q)
+        self.lse = torch.empty((layers, B, 32), dtype=torch.float32, device=self.d0)
+        self.num_ctas = ops.default_ctas(0)
+        self.ws = torch.zeros(ops.decode_workspace_size(B, self.num_ctas), dtype=torch.uint8, device=self.d0)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.d0)
+        self.scale = 128 ** -0.5
+        self.peer_k = [[self.bank.banks[0][i, 0]] for i in range(layers)]
+        self.peer_v = [[self.bank.banks[0][i, 1]] for i in range(layers)]
+        if migrate:
+            self.lp = local_plane_pointers(list(zip(self.k, self.v)), self.d0)
+            self.rp = self.bank.pointers.to(self.d0)
+            self.copy_stream = torch.cuda.Stream(self.d0)
+            self.mig_status = torch.zeros(1, dtype=torch.int32, device=self.d0)
+            self.mig_events = []
+            self.batch_no = 0
+            self.pending = None
+
+    def _launch_migration(self):
+        """Async copy of the next 2048 background slots (all resident planes) on the side stream."""
+        k = self.batch_no % 4
+        src = self.bg_local[k * self.mig_tokens:(k + 1) * self.mig_tokens]
+        dst = self.bg_remote[k * self.mig_tokens:(k + 1) * self.mig_tokens]
+        start = torch.cuda.Event(enable_timing=True)
+        done = torch.cuda.Event(enable_timing=True)
+        self.copy_stream.wait_stream(torch.cuda.current_stream(self.d0))
+        with torch.cuda.stream(self.copy_stream):
+            start.record(self.copy_stream)
+            self.ops.migrate_copy(self.lp, self.rp, 2 * self.layers, 1, src, dst, False, self.C + 1, self.R_cap,
+                                  self.mig_status, max_ctas=32)
+            done.record(self.copy_stream)
+        self.mig_events.append((start, done))
+        self.pending = (k, done)
+        self.batch_no += 1
+
+    def _commit_migration(self):
+        """Step boundary: the main stream waits for the copy, then switches the background rows' tables."""
+        if self.pending is None:
+            return
+        k, done = self.pending
+        torch.cuda.current_stream(self.d0).wait_event(done)
+        n = self.mig_tokens
+        self.tier[self.B, k * n:(k + 1) * n] = 1
+        self.slot[self.B, k * n:(k + 1) * n] = self.bg_remote[k * n:(k + 1) * n].to(torch.int32)
+        self.pending = None
+
+    def step(self, events=None):
+        ops = self.ops
+        if self.migrate:
+            self._commit_migration()
+        ops.pack_read_order(self.tier, self.slot, self.req, self.seq, self.C, self.RN, self.TN, self.indices,
+                            status=self.status)
+        if self.migrate:
+            self._launch_migration()
+        for i in range(self.layers):
+            if events is not None:
+                events[i][0].record()
+            ops.tiered_decode(self.q[i], self.k[i], self.v[i], self.C, self.peer_k[i], self.peer_v[i], self.indptr,
+                              self.indices, self.scale, self.out[i], self.lse[i], self.ws, self.num_ctas)
+            if events is not None:
+                events[i][1].record()
+
+    def local_bytes(self):
+        return 4096 * (self.T - self.R) + 8192 * self.B * 2 + 128 * self.B
+
+    def remote_bytes(self):
+        return 4096 * self.R
+
+
+def run_tiered(args):
+    if torch.cuda.device_count() < 2:
+        print(json.dumps({"metric": METRIC, "unavailable": f"{args.workload} needs 2 GPUs"}))
+        return
+    w = TieredWorkload(args)
+    stream = torch.cuda.current_stream(w.d0)
+    for _ in range(max(args.warmup, 3)):
+        w.step()
+    torch.cuda.synchronize(w.d0)
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]))
+    clocks.start()
+    time.sleep(0.3)
+    if w.migrate:
+        w.mig_events = []
+    all_events = []
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(w.layers)]
+        w.step(ev)
+        all_events.append(ev)
+    t1.record(stream)
+    torch.cuda.synchronize(w.d0)
+    torch.cuda.synchronize(w.d1)
+    clk = clocks.stop()
+    layer_ms = [a.elapsed_time(b) for ev in all_events for a, b in ev]
+    t_layer = sum(layer_ms) / len(layer_ms) / 1e3
+    peak_hbm, peak_kind = measured_peaks()
+    t_local = w.local_bytes() / (peak_hbm * 1e9)
+    t_remote = w.remote_bytes() / (PEER_GBS * 1e9)
+    t_star = max(t_local, t_remote)
+    tok_s = w.B / (36 * t_layer)
+    status = int(w.status.item()) | int(w.ws[:4].view(torch.int32).item())
+    result = {
+        "metric": METRIC, "value": round(tok_s, 2), "unit": UNIT, "n_gpus": 2, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(36 * t_layer * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: 1 compute GPU + 1 KV supplier GPU (peer access), tiered decode",
+                   "batch": w.B, "sum_kv_tokens": w.T, "remote_tokens": w.R,
+                   "remote_over_local": round(w.R / (w.T - w.R), 4), "read_order_rn_tn": [w.RN, w.TN],
+                   "layers_resident": w.layers, "per_step": "36 x per-layer time",
+                   "concurrent_migration": bool(w.migrate)},
+        "roofline": {"bound": "nvlink" if t_remote > t_local else "hbm",
+                     "achieved": round((w.local_bytes() + w.remote_bytes()) / t_layer / 1e9, 1),
+                     "peak": round((w.local_bytes() + w.remote_bytes()) / t_star / 1e9, 1), "unit": "GB/s",
+                     "frac": round(t_star / t_layer, 4), "traffic": None,
+                     "local_gbs": round(w.local_bytes() / t_layer / 1e9, 1),
+                     "peer_gbs": round(w.remote_bytes() / t_layer / 1e9, 1),
+                     "t_star_ms": round(t_star * 1e3, 4), "layer_ms": round(t_layer * 1e3, 4),
+                     "peak_source": f"{peak_kind} hbm_gbs {peak_hbm} + peer copy {PEER_GBS} GB/s per direction"},
+        "gpu_launches": (1 + 2 * w.layers + (1 if w.migrate else 0)) * args.steps,
+        "device_status": status,
+    }
+    if w.migrate and w.mig_events:
+        mig_ms = [a.elapsed_time(b) for a, b in w.mig_events]
+        nbytes = w.mig_tokens * w.layers * 4096
+        result["migration"] = {"tokens_per_batch": w.mig_tokens, "planes": 2 * w.layers,
+                               "bytes_per_batch": nbytes, "bytes_per_batch_36_layers": w.mig_tokens * 147456,
+                               "avg_ms": round(sum(mig_ms) / len(mig_ms), 4),
+                               "gbs": round(nbytes / (sum(mig_ms) / len(mig_ms) / 1e3) / 1e9, 1),
+                               "status": int(w.mig_status.item())}
+        # bit-exactness of everything migrated so far (sampled rows of every plane)
+        torch.cuda.synchronize(w.d0)
+        k = min(w.batch_no, 4) * w.mig_tokens
+        ok = True
+        for i in range(w.layers):
+            for plane, t in enumerate((w.k[i], w.v[i])):
+                src = w.bg_local[:k:97]
+                dst = w.bg_remote[:k:97]
+                got = w.bank.banks[0][i, plane].index_select(0, dst.to(w.d1)).to(w.d0)
+                ok &= bool(torch.equal(got.view(torch.int16), t.index_select(0, src).view(torch.int16)))
+        result["migration"]["bit_exact_sampled"] = ok
+    if clk:
+        result["clocks"] = clk
+    print(json.dumps(result), flush=True)
+
 # -------------------------------------------------------------- reference arm
 def run_reference(args):
     """The reference's CPU attention math (fp32 torch restatement of check_attention_output,
@@ -413,6 +628,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload in TIERED:
+        run_tiered(args)
     else:
         run_dual(args)
 
