@@ -1,7 +1,7 @@
-"""Benchmark of the tiered paged-decode hot path (BASELINE metric: paged-decode tok/s and
+"""Benchmark of the tiered paged-decode hot path (headline metric: paged-decode tok/s and
 local+peer GB/s as % of roofline).
 
-Default workload (one B200, all-local): a full 36-layer
+Default workload (headline config 2: one B200, all-local): a full 36-layer
 Qwen3-8B-shaped KV pool of 1,048,576 token slots per plane (72 planes x 2 KiB
 x (C+1) slots = 154.6 GB in HBM), batch 64, KV lengths uniform in [2048, 32768]
 (seeded; redrawn with the next seed while the sum exceeds the pool), slots a
@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["dual", "reference"], default="dual")
-    ap.add_argument("--workload", choices=list(WORKLOADS) + list(TIERED), default="config2")
+    ap.add_argument("--workload", choices=list(WORKLOADS) + list(TIERED) + ["migration"], default="config2")
     ap.add_argument("--seed", type=int, default=20261101)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -167,6 +167,7 @@ class DecodeWorkload:
     def step(self, events=None):
         ops = self.ops
         ops.pack_read_order(self.tier, self.slot, self.req, self.seq, self.C, 5, 32, self.indices, status=self.status)
+        torch.cuda.nvtx.range_push("decode_layers")
         for i in range(self.layers):
             if events is not None:
                 events[i][0].record()
@@ -174,6 +175,7 @@ class DecodeWorkload:
                               self.out[i], self.lse[i], self.ws, self.num_ctas)
             if events is not None:
                 events[i][1].record()
+        torch.cuda.nvtx.range_pop()
 
     def bytes_per_layer(self):
         return 4096 * self.T + 8192 * self.B * 2 + 128 * self.B
@@ -578,6 +580,43 @@ def run_tiered(args):
         result["clocks"] = clk
     print(json.dumps(result), flush=True)
 
+
+# ------------------------------------------------------------ migration copy (1 GPU)
+def run_migration(args):
+    """One 2048-slot migration batch over all 72 planes (36 layers x K, V = 302 MB) from the local
+    pool into a supplier-bank layout on the same GPU, repeated; bytes moved / CUDA-event time."""
+    from dual_b200 import ops
+    from dual_b200.remote_bank import RemoteBank, local_plane_pointers
+    dev = torch.device("cuda:0")
+    layers, lslots, bslots, n = 36, 1 << 16, 1 << 13, 2048
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    local = [(torch.randn((lslots + 1, 8, 128), generator=g, device=dev).to(torch.bfloat16),
+              torch.randn((lslots + 1, 8, 128), generator=g, device=dev).to(torch.bfloat16)) for _ in range(layers)]
+    bank = RemoteBank([torch.zeros((layers, 2, bslots, 8, 128), dtype=torch.bfloat16, device=dev)])
+    lp = local_plane_pointers(local, dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    src = (torch.randperm(lslots, generator=g, device=dev)[:n] + 1).long()
+    dst = torch.randperm(bslots, generator=g, device=dev)[:n].long()
+    for _ in range(max(args.warmup, 3)):
+        ops.migrate_copy(lp, bank.pointers, 72, 1, src, dst, False, lslots + 1, bslots, status)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        ops.migrate_copy(lp, bank.pointers, 72, 1, src, dst, False, lslots + 1, bslots, status)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    nbytes = n * 147456
+    ok = all(torch.equal(bank.gather(i, p, dst).view(torch.int16), local[i][p].index_select(0, src).view(torch.int16))
+             for i in range(0, layers, 7) for p in range(2))
+    peak, kind = measured_peaks()
+    print(json.dumps({"metric": "migration copy GB/s (2048 slots x 72 planes)", "value": round(nbytes / ms / 1e6, 1),
+                      "unit": "GB/s moved", "ms_per_batch": round(ms, 4), "bytes_per_batch": nbytes,
+                      "roofline": {"bound": "hbm", "achieved": round(2 * nbytes / ms / 1e6, 1), "peak": peak,
+                                   "unit": "GB/s (read+write)", "frac": round(2 * nbytes / ms / 1e6 / peak, 4)},
+                      "bit_exact_sampled": ok, "status": int(status.item()), "gpu_launches": args.steps}), flush=True)
+
 # -------------------------------------------------------------- reference arm
 def run_reference(args):
     """The reference's CPU attention math (fp32 torch restatement of check_attention_output,
@@ -630,6 +669,8 @@ def main():
         run_reference(args)
     elif args.workload in TIERED:
         run_tiered(args)
+    elif args.workload == "migration":
+        run_migration(args)
     else:
         run_dual(args)
 

@@ -5,7 +5,7 @@ the generator script (run where the reference is mounted) and the tests (run
 here and on the GPU box, same torch build) see bit-identical inputs.
 
 Cases:
-  * ``config1``: one Qwen3-8B-shaped decode layer, 4 requests
+  * ``config1`` -- the CPU reference config 1: one Qwen3-8B-shaped decode layer, 4 requests
     with L = 512/1024/2048/4096, slots from a seeded permutation of a 16,384-slot
     pool, the last floor(0.1 L) positions of each request remote, stored in a
     second (supplier) pool; Q, K, V ~ N(0, 1) in bf16.

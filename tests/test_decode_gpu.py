@@ -1,6 +1,6 @@
 """Parity of the tiered split-KV decode kernel (through the C ABI) against the pinned oracle.
 
-Tolerance: bf16 outputs within 2e-3 abs / 1e-2 rel of the fp32 reference;
+Tolerance (the hot path's parity target): bf16 outputs within 2e-3 abs / 1e-2 rel of the fp32 reference;
 LSE (base 2) within the same bound.
 """
 import numpy as np
