@@ -57,7 +57,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["dual", "reference"], default="dual")
-    ap.add_argument("--workload", choices=list(WORKLOADS) + list(TIERED) + ["migration"], default="config2")
+    ap.add_argument("--workload", choices=list(WORKLOADS) + list(TIERED) + ["migration"] + list(APPEND),
+                    default="config2")
     ap.add_argument("--seed", type=int, default=20261101)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -617,6 +618,103 @@ def run_migration(args):
                                    "unit": "GB/s (read+write)", "frac": round(2 * nbytes / ms / 1e6 / peak, 4)},
                       "bit_exact_sampled": ok, "status": int(status.item()), "gpu_launches": args.steps}), flush=True)
 
+
+# ------------------------------------------------------------ causal append (config 4 shapes)
+APPEND = {
+    # name: (requests, qmin, qmax (log-uniform), Pmin, Pmax (uniform), remote/local, suppliers)
+    "config4": (32, 128, 2048, 4096, 32768, 0.1797, 3),
+    "append-small": (4, 128, 512, 1024, 4096, 0.1797, 3),
+}
+
+
+def run_append(args):
+    """Causal append attention of one layer for the 4-GPU configuration's shapes: per request a
+    history prefix of P tokens (remote share R/L = 17.97 %, one request in eight ~95 % remote, remote
+    only in the history) and q new tokens.  Supplier banks live on GPUs 1..3 when present (peer
+    access), else in this GPU's memory.  FLOPs per request = 16384 (q P + q (q + 1) / 2)."""
+    from dual_b200 import ops, topology
+    B, qmin, qmax, pmin, pmax, rl, nsup = APPEND[args.workload]
+    dev = torch.device("cuda:0")
+    ngpu = torch.cuda.device_count()
+    owners = [torch.device(f"cuda:{1 + i % (ngpu - 1)}") if ngpu > 1 else dev for i in range(nsup)]
+    for o in set(owners):
+        if o != dev:
+            topology.enable_peer(0, o.index)
+    rng = np.random.default_rng(args.seed)
+    qlens = np.exp(rng.uniform(np.log(qmin), np.log(qmax), B)).astype(np.int64)
+    pref = rng.integers(pmin, pmax + 1, B).astype(np.int64)
+    lengths = pref + qlens
+    frac = np.full(B, rl / (1 + rl))
+    heavy = np.arange(B) % 8 == 0
+    frac[heavy] = 0.95
+    frac[~heavy] = max(0.0, (rl / (1 + rl) * lengths.sum() - 0.95 * lengths[heavy].sum()) / lengths[~heavy].sum())
+    remote = np.minimum((frac * lengths).astype(np.int64), pref)
+    T, R = int(lengths.sum()), int(remote.sum())
+    C = T - R + 1
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    k = torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    v = torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    per_bank = R // nsup + 1
+    pk = [torch.randn((per_bank, 8, 128), device=o).to(torch.bfloat16) for o in owners]
+    pv = [torch.randn((per_bank, 8, 128), device=o).to(torch.bfloat16) for o in owners]
+    tier = torch.zeros((B, int(lengths.max())), dtype=torch.int32, device=dev)
+    slot = torch.zeros_like(tier)
+    perm = (torch.randperm(C, generator=g, device=dev) + 1).to(torch.int32)
+    off, roff = 0, 0
+    for b in range(B):
+        L, r = int(lengths[b]), int(remote[b])
+        far = torch.zeros(L, dtype=torch.bool)
+        far[torch.from_numpy(np.sort(rng.choice(int(pref[b]), r, replace=False)))] = True
+        s_ = torch.empty(L, dtype=torch.int32)
+        s_[far] = torch.arange(roff, roff + r, dtype=torch.int32)
+        s_[~far] = perm[off:off + L - r].cpu()
+        off += L - r
+        roff += r
+        tier[b, :L] = far.to(torch.int32).to(dev)
+        slot[b, :L] = s_.to(dev)
+    req = torch.arange(B, dtype=torch.int32, device=dev)
+    seq = torch.tensor(lengths, dtype=torch.int32, device=dev)
+    pre = torch.tensor(pref, dtype=torch.int32, device=dev)
+    full = torch.empty(T, dtype=torch.int32, device=dev)
+    ops.pack_read_order(tier, slot, req, seq, C, 5, 32, full, prefix_lens=pre)
+    qo = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    kv = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    work = ops.append_plan(qo, kv, True).to(dev)
+    Q = int(qlens.sum())
+    q = torch.empty((Q, 32, 128), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    out = torch.empty_like(q)
+    lse = torch.empty((Q, 32), dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    qo_d, kv_d = torch.from_numpy(qo).to(dev), torch.from_numpy(kv).to(dev)
+
+    def step():
+        ops.tiered_append(q, k, v, C, pk, pv, qo_d, kv_d, full, True, 128 ** -0.5, work, out, lse, status)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b_.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b_) / args.steps
+    flops = float(sum(16384 * (int(x) * int(p_) + int(x) * (int(x) + 1) / 2) for x, p_ in zip(qlens, pref)))
+    tf = flops / (ms / 1e3) / 1e12
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    print(json.dumps({"metric": "causal append attention time per layer", "value": round(ms, 4), "unit": "ms",
+                      "higher_is_better": False, "tflops": round(tf, 1),
+                      "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                                   "frac": round(tf / peak, 4),
+                                   "peak_source": "measured" if peaks else "fallback"},
+                      "config": {"workload": args.workload, "requests": B, "sum_q": Q, "sum_kv": T,
+                                 "remote_tokens": R, "remote_over_local": round(R / (T - R), 4),
+                                 "suppliers": [str(o) for o in owners], "work_items": int(work.shape[0]),
+                                 "flops_per_layer": flops},
+                      "status": int(status.item()), "gpu_launches": args.steps}), flush=True)
+
 # -------------------------------------------------------------- reference arm
 def run_reference(args):
     """The reference's CPU attention math (fp32 torch restatement of check_attention_output,
@@ -671,6 +769,8 @@ def main():
         run_tiered(args)
     elif args.workload == "migration":
         run_migration(args)
+    elif args.workload in APPEND:
+        run_append(args)
     else:
         run_dual(args)
 

@@ -7,7 +7,7 @@ the FlashInfer wrapper API the reference patches (``wrapper``) and a C ABI
 (``include/dual_b200.h``, library ``dual_b200/lib/libdual_b200.so``).
 """
 from . import _lib, ops  # noqa: F401
-from .wrapper import BatchDecodeWithPagedKVCacheWrapper, activate  # noqa: F401
+from .wrapper import BatchDecodeWithPagedKVCacheWrapper, BatchPrefillWithPagedKVCacheWrapper, activate  # noqa: F401
 from .remote_bank import RemoteBank, local_plane_pointers  # noqa: F401
 
-__all__ = ["BatchDecodeWithPagedKVCacheWrapper", "activate", "RemoteBank", "local_plane_pointers", "ops"]
+__all__ = ["BatchDecodeWithPagedKVCacheWrapper", "BatchPrefillWithPagedKVCacheWrapper", "activate", "RemoteBank", "local_plane_pointers", "ops"]

@@ -46,6 +46,16 @@ SIGNATURES = {
         VP, C.c_int64, C.c_int64, VP,          # out, strides, lse
         VP, C.c_int,                           # status (nullable), num_ctas
         C.c_int, VP]),                         # device, stream
+    "dual_append_plan": (C.c_int, [VP, VP, C.c_int, C.c_int, VP, C.c_int64, C.POINTER(C.c_int64)]),
+    "dual_tiered_append": (C.c_int, [
+        VP, C.c_int64, C.c_int64,              # q, strides
+        VP, VP, C.c_int64, C.c_int64,          # k_local, v_local, local stride, capacity
+        C.POINTER(VP), C.POINTER(VP), C.c_int,  # peer_k, peer_v, num_peers
+        C.c_int64, C.c_int64,                  # peer stride, peer slots
+        VP, VP, VP, C.c_int64, C.c_int, C.c_int,  # qo_indptr, kv_indptr, indices, num_indices, batch, causal
+        C.c_double, VP, C.c_int64,             # sm_scale, work, num_work
+        VP, C.c_int64, C.c_int64, VP,          # out, strides, lse
+        VP, C.c_int, VP]),                     # status, device, stream
     "dual_pack_read_order": (C.c_int, [
         VP, VP, C.c_int64, C.c_int64, VP, VP, VP, VP, C.c_int, C.c_int64, C.c_int, C.c_int, VP, VP, VP, C.c_int, VP]),
     "dual_write_prefill_layout": (C.c_int, [

@@ -17,7 +17,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIBDIR = PKG / "lib"
 LIBNAME = "libdual_b200.so"
-SOURCES = ["capi.cu", "decode.cu", "decode_noalloc.cu", "pack.cu", "migrate.cu"]
+SOURCES = ["capi.cu", "decode.cu", "decode_noalloc.cu", "pack.cu", "migrate.cu", "prefill.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -9,6 +9,7 @@
 #include "decode.cuh"
 #include "migrate.cuh"
 #include "pack.cuh"
+#include "prefill.cuh"
 
 namespace {
 
@@ -132,6 +133,87 @@ int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.lse = lse;
   cudaError_t e = dual::launch_tiered_decode(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tiered decode launch");
+  return DUAL_OK;
+}
+
+int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, int batch, int causal,
+                     int32_t* work_host, int64_t max_work, int64_t* num_work) {
+  g_last_error.clear();
+  if (batch < 0 || !num_work) return fail(DUAL_EINVAL, "bad append plan arguments");
+  if (batch > 0 && (!qo_indptr_host || !kv_indptr_host)) return fail(DUAL_EINVAL, "null indptr");
+  for (int b = 0; b < batch; ++b) {
+    const int64_t ql = int64_t(qo_indptr_host[b + 1]) - qo_indptr_host[b];
+    const int64_t kl = int64_t(kv_indptr_host[b + 1]) - kv_indptr_host[b];
+    if (ql < 0 || kl < 0) return fail(DUAL_EINVAL, "request %d: negative length", b);
+    if (causal && kl < ql) return fail(DUAL_EINVAL, "request %d: causal append needs kv length >= query length", b);
+  }
+  *num_work = dual::append_plan(qo_indptr_host, kv_indptr_host, batch, causal, work_host, max_work);
+  return DUAL_OK;
+}
+
+int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_local,
+                       const void* v_local, int64_t local_stride_bytes, int64_t local_capacity,
+                       const void* const* peer_k, const void* const* peer_v, int num_peers,
+                       int64_t peer_stride_bytes, int64_t peer_slots, const int32_t* qo_indptr,
+                       const int32_t* kv_indptr, const int32_t* unified_indices, int64_t num_indices, int batch,
+                       int causal, double sm_scale, const int32_t* work, int64_t num_work, void* out,
+                       int64_t out_stride_token, int64_t out_stride_head, float* lse, uint32_t* status, int device,
+                       void* stream) {
+  g_last_error.clear();
+  if (batch < 0 || num_work < 0) return fail(DUAL_EINVAL, "negative batch or work count");
+  if (batch == 0 || num_work == 0) return DUAL_OK;
+  if (num_work > 0x7fffffffLL) return fail(DUAL_EINVAL, "too many work items");
+  if (!q || !k_local || !v_local || !qo_indptr || !kv_indptr || !unified_indices || !work || !out || !status)
+    return fail(DUAL_EINVAL, "null pointer argument");
+  if (num_peers < 0 || num_peers > dual::kMaxPeers) return fail(DUAL_EINVAL, "num_peers out of range");
+  const int64_t min_stride = int64_t(dual::kNumKvHeads) * dual::kHeadDim * 2;
+  if (!aligned16(k_local) || !aligned16(v_local) || (local_stride_bytes & 15) || local_stride_bytes < min_stride)
+    return fail(DUAL_EINVAL, "local pool must be 16-byte aligned with a slot stride >= 2048 B, multiple of 16");
+  if (local_capacity < 0 || local_capacity > 0xfffffffeLL) return fail(DUAL_EINVAL, "local_capacity out of range");
+  if ((q_stride_head % 8) || (q_stride_token % 8) || (out_stride_head % 8) || (out_stride_token % 8) ||
+      !aligned16(q) || !aligned16(out))
+    return fail(DUAL_EINVAL, "q/out must be 16-byte aligned with element strides that are multiples of 8");
+  if (num_peers > 0) {
+    if (!peer_k || !peer_v) return fail(DUAL_EINVAL, "peer pointer arrays are null");
+    if ((peer_stride_bytes & 15) || peer_stride_bytes < min_stride || peer_slots <= 0)
+      return fail(DUAL_EINVAL, "peer banks need a 16-byte multiple slot stride >= 2048 B and slots > 0");
+    for (int i = 0; i < num_peers; ++i)
+      if (!peer_k[i] || !peer_v[i] || !aligned16(peer_k[i]) || !aligned16(peer_v[i]))
+        return fail(DUAL_EINVAL, "peer bank %d pointer null or not 16-byte aligned", i);
+  }
+  if (!(sm_scale > 0.0)) return fail(DUAL_EINVAL, "sm_scale must be positive");
+  if (int rc = set_device(device)) return rc;
+  dual::AppendParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_stride_tok = q_stride_token;
+  p.q_stride_head = q_stride_head;
+  p.k_local = static_cast<const char*>(k_local);
+  p.v_local = static_cast<const char*>(v_local);
+  p.local_stride = local_stride_bytes;
+  p.local_capacity = local_capacity;
+  for (int i = 0; i < dual::kMaxPeers; ++i) {
+    p.peer_k[i] = i < num_peers ? static_cast<const char*>(peer_k[i]) : nullptr;
+    p.peer_v[i] = i < num_peers ? static_cast<const char*>(peer_v[i]) : nullptr;
+  }
+  p.num_peers = num_peers;
+  p.peer_stride = peer_stride_bytes;
+  p.peer_slots = peer_slots;
+  p.qo_indptr = qo_indptr;
+  p.kv_indptr = kv_indptr;
+  p.indices = unified_indices;
+  p.num_indices = num_indices < 0 ? 0 : num_indices;
+  p.batch = batch;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = static_cast<float>(sm_scale * 1.4426950408889634);
+  p.work = reinterpret_cast<const int4*>(work);
+  p.num_work = int(num_work);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_tok = out_stride_token;
+  p.out_stride_head = out_stride_head;
+  p.lse = lse;
+  p.status = status;
+  cudaError_t e = dual::launch_tiered_append(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tiered append launch");
   return DUAL_OK;
 }
 

@@ -150,6 +150,17 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Split two fp32 values into bf16 pairs hi + lo with hi = rn(x), lo = rn(x - hi): the sum carries
+// ~16 significant bits, so a probability matrix fed to a bf16 MMA twice (hi, then lo) loses
+// almost nothing to the bf16 rounding of P.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
 // Hardware base-2 exponential (MUFU.EX2 via the PTX ex2.approx instruction).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

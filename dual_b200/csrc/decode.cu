@@ -252,16 +252,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __
       for (int nt = 0; nt < 16; ++nt) {
         o[nt][0] *= alpha;
         o[nt][1] *= alpha;
+        o[nt][2] *= alpha;
+        o[nt][3] *= alpha;
       }
-      const uint32_t pa0 = pack_bf16x2(pr[0], pr[1]);
-      const uint32_t pa2 = pack_bf16x2(pr[2], pr[3]);
+      // P as a hi + lo pair of bf16 values, keeping P's bf16 rounding out of the output: hi feeds
+      // MMA rows g (the 4 query heads), lo feeds the otherwise idle rows g + 8 of the same MMA;
+      // the two accumulator halves are added when the segment is flushed.
+      uint32_t pa0, pa2, pl0, pl2;
+      split_bf16x2(pr[0], pr[1], pa0, pl0);
+      split_bf16x2(pr[2], pr[3], pa2, pl2);
       // ---- O += P V
 #pragma unroll
       for (int dp = 0; dp < 8; ++dp) {
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4_trans(b0, b1, b2, b3, sV + ((mi & 1) * 8 + rr) * Cfg::PITCH + (dp * 16 + (mi >> 1) * 8) * 2);
-        mma_bf16_16816(o[2 * dp], pa0, 0u, pa2, 0u, b0, b1);
-        mma_bf16_16816(o[2 * dp + 1], pa0, 0u, pa2, 0u, b2, b3);
+        mma_bf16_16816(o[2 * dp], pa0, pl0, pa2, pl2, b0, b1);
+        mma_bf16_16816(o[2 * dp + 1], pa0, pl0, pa2, pl2, b2, b3);
       }
     }
     __syncwarp();
@@ -275,7 +281,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __
         float* dst = p.partial + (int64_t(g + cur_b) * Cfg::ROWS + h * kGqa + gi) * kPartialStride;
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt)
-          *reinterpret_cast<float2*>(dst + nt * 8 + 2 * ci) = make_float2(o[nt][0], o[nt][1]);
+          *reinterpret_cast<float2*>(dst + nt * 8 + 2 * ci) = make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
         if (ci == 0) *reinterpret_cast<float2*>(dst + kHeadDim) = make_float2(m_run, d_row);
       }
       reset_state();

@@ -104,6 +104,51 @@ def tiered_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
         dev, _stream(q.device)))
 
 
+def append_plan(qo_indptr, kv_indptr, causal: bool) -> torch.Tensor:
+    """Host-side work list (request, kv head, 32-token query tile, cost), costliest first, as an int32
+    CPU tensor [n, 4].  ``qo_indptr`` / ``kv_indptr``: host sequences or CPU tensors."""
+    qo = torch.as_tensor(qo_indptr, dtype=torch.int32).cpu().contiguous()
+    kv = torch.as_tensor(kv_indptr, dtype=torch.int32).cpu().contiguous()
+    B = qo.numel() - 1
+    lib = _lib.load()
+    n = C.c_int64(0)
+    _lib.check(lib.dual_append_plan(qo.data_ptr(), kv.data_ptr(), B, int(bool(causal)), None, 0, C.byref(n)))
+    work = torch.empty((max(n.value, 1), 4), dtype=torch.int32)
+    _lib.check(lib.dual_append_plan(qo.data_ptr(), kv.data_ptr(), B, int(bool(causal)), work.data_ptr(), n.value,
+                                    C.byref(n)))
+    return work[: n.value]
+
+
+def tiered_append(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor, local_capacity: int,
+                  peer_k: Sequence[torch.Tensor], peer_v: Sequence[torch.Tensor], qo_indptr: torch.Tensor,
+                  kv_indptr: torch.Tensor, unified_indices: torch.Tensor, causal: bool, sm_scale: float,
+                  work: torch.Tensor, out: torch.Tensor, lse: Optional[torch.Tensor], status: torch.Tensor) -> None:
+    """Causal (or non-causal) append attention over the tiered pool; ``work`` from ``append_plan`` on the device."""
+    dev = _dev(q)
+    _check(q.dtype == torch.bfloat16 and q.dim() == 3 and tuple(q.shape[1:]) == (NUM_QO_HEADS, HEAD_DIM)
+           and q.stride(2) == 1, "q must be bf16 [sum q, 32, 128]")
+    _check(out.dtype == torch.bfloat16 and out.shape == q.shape and out.stride(2) == 1, "out must match q")
+    _check(qo_indptr.dtype == torch.int32 and kv_indptr.dtype == torch.int32 and unified_indices.dtype == torch.int32,
+           "indptrs / indices must be int32")
+    _check(work.dtype == torch.int32 and work.is_contiguous() and work.device == q.device, "work must be int32 on the device")
+    if lse is not None:
+        _check(lse.dtype == torch.float32 and lse.is_contiguous(), "lse must be contiguous fp32 [sum q, 32]")
+    ls = _pool_stride(k_local, "k_local")
+    _check(_pool_stride(v_local, "v_local") == ls, "k/v local pools must share a slot stride")
+    n = len(peer_k)
+    pk = (C.c_void_p * max(n, 1))(*[t.data_ptr() for t in peer_k])
+    pv = (C.c_void_p * max(n, 1))(*[t.data_ptr() for t in peer_v])
+    ps = _pool_stride(peer_k[0], "peer_k0") if n else 0
+    slots = peer_k[0].shape[0] if n else 0
+    lib = _lib.load()
+    _lib.check(lib.dual_tiered_append(
+        q.data_ptr(), q.stride(0), q.stride(1), k_local.data_ptr(), v_local.data_ptr(), ls, int(local_capacity),
+        pk, pv, n, ps, slots, qo_indptr.data_ptr(), kv_indptr.data_ptr(), unified_indices.data_ptr(),
+        unified_indices.numel(), qo_indptr.numel() - 1, int(bool(causal)), float(sm_scale), work.data_ptr(),
+        work.shape[0], out.data_ptr(), out.stride(0), out.stride(1), _ptr(lse), status.data_ptr(), dev,
+        _stream(q.device)))
+
+
 def pack_read_order(tier: torch.Tensor, slot: torch.Tensor, req_pool_indices: torch.Tensor,
                     seq_lens: torch.Tensor, local_capacity: int, remote_rows: int, tile_rows: int,
                     full_out: torch.Tensor, prefix_lens: Optional[torch.Tensor] = None,

@@ -134,6 +134,84 @@ class BatchDecodeWithPagedKVCacheWrapper:
     run_return_lse = functools.partialmethod(run, return_lse=True)
 
 
+class BatchPrefillWithPagedKVCacheWrapper:
+    """Paged append / prefill attention (page_size 1, NHD), FlashInfer's plan/run convention.
+
+    ``plan`` takes the (host or device) ``qo_indptr`` / ``paged_kv_indptr`` like FlashInfer's planner,
+    builds the costliest-first work list on the host and uploads it; ``run`` launches the tcgen05
+    append kernel.  The reference passes the same tiered tail as for decode
+    (peer/prefill_backend.py:25-37): ``run(q, paged_kv, *peers, indices, local_capacity, sm_scale)``,
+    where ``indices`` is the packer's Full list (causal, non-ragged) or History list (ragged cascade).
+    """
+
+    def __init__(self, float_workspace_buffer: torch.Tensor, kv_layout: str = "NHD", use_cuda_graph: bool = False,
+                 qo_indptr_buf=None, paged_kv_indptr_buf=None, paged_kv_indices_buf=None,
+                 paged_kv_last_page_len_buf=None, custom_mask_buf=None, mask_indptr_buf=None,
+                 backend: str = "auto", jit_args=None):
+        if kv_layout != "NHD":
+            raise ValueError("only the NHD layout is supported")
+        self.device = float_workspace_buffer.device
+        self._float_workspace = float_workspace_buffer
+        self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._plan = None
+        self._custom_mask_buf = None
+        self._window_left = -1
+        self._jit_module = None
+        self._jit_additional_tensor_names = list(TENSORS)
+        self._jit_additional_scalar_names = list(SCALARS)
+
+    def plan(self, qo_indptr, paged_kv_indptr, paged_kv_indices, paged_kv_last_page_len, num_qo_heads: int,
+             num_kv_heads: int, head_dim_qk: int, page_size: int, head_dim_vo: Optional[int] = None,
+             custom_mask=None, packed_custom_mask=None, causal: bool = False, pos_encoding_mode: str = "NONE",
+             use_fp16_qk_reduction: bool = False, sm_scale: Optional[float] = None, window_left: int = -1,
+             logits_soft_cap: Optional[float] = None, rope_scale=None, rope_theta=None, q_data_type="bfloat16",
+             kv_data_type=None, non_blocking: bool = True, **kwargs) -> None:
+        if (num_qo_heads, num_kv_heads, head_dim_qk, page_size) != (ops.NUM_QO_HEADS, ops.NUM_KV_HEADS,
+                                                                    ops.HEAD_DIM, 1):
+            raise ValueError("dual_b200 append is built for 32 q heads, 8 kv heads, head_dim 128, page_size 1")
+        if head_dim_vo not in (None, head_dim_qk):
+            raise ValueError("head_dim_vo must equal head_dim_qk")
+        if custom_mask is not None or packed_custom_mask is not None or window_left != -1 or \
+                logits_soft_cap not in (None, 0, 0.0) or pos_encoding_mode != "NONE":
+            raise ValueError("only DefaultAttention (causal or not; no custom mask, window, soft cap, RoPE fusion)")
+        qo_h = torch.as_tensor(qo_indptr).to("cpu", torch.int32)
+        kv_h = torch.as_tensor(paged_kv_indptr).to("cpu", torch.int32)
+        work = ops.append_plan(qo_h, kv_h, causal)
+        self._plan = dict(qo=qo_h.to(self.device, non_blocking=non_blocking),
+                          kv=kv_h.to(self.device, non_blocking=non_blocking),
+                          indices=torch.as_tensor(paged_kv_indices).to(self.device, torch.int32),
+                          work=work.to(self.device, non_blocking=non_blocking), causal=bool(causal),
+                          total_q=int(qo_h[-1]), batch=qo_h.numel() - 1,
+                          sm_scale=float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(head_dim_qk))
+
+    def run(self, q: torch.Tensor, paged_kv_cache, *args, q_scale=None, k_scale=None, v_scale=None,
+            out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None, return_lse: bool = False,
+            enable_pdl=None, window_left=None, **kwargs):
+        if self._plan is None:
+            raise RuntimeError("plan() must be called before run()")
+        pl = self._plan
+        k, v = _unpack_paged_kv(paged_kv_cache)
+        if args:
+            peer_k, peer_v, indices, capacity, scale = split_tiered_args(args)
+        else:
+            peer_k, peer_v, indices, capacity, scale = [], [], pl["indices"], k.shape[0] - 1, pl["sm_scale"]
+        if q.shape[0] != pl["total_q"]:
+            raise ValueError(f"q has {q.shape[0]} rows, plan() was for {pl['total_q']}")
+        if out is None:
+            out = torch.empty_like(q)
+        if return_lse and lse is None:
+            lse = torch.empty((q.shape[0], ops.NUM_QO_HEADS), dtype=torch.float32, device=q.device)
+        ops.tiered_append(q, k, v, capacity, peer_k, peer_v, pl["qo"], pl["kv"], indices, pl["causal"], scale,
+                          pl["work"], out, lse if return_lse else None, self._status)
+        return (out, lse) if return_lse else out
+
+    run_return_lse = functools.partialmethod(run, return_lse=True)
+
+    def status(self) -> int:
+        """Device status bits accumulated by this wrapper's launches (synchronous read)."""
+        return ops.status_read(self._status)
+
+
 def activate(wrapper):
     """Compatibility shim for the reference's ``flashinfer_peer.activate`` (peer/flashinfer_peer.py:145-150).
 

@@ -103,6 +103,32 @@ int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_
                                void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
                                uint32_t* status, int num_ctas, int device, void* stream);
 
+/* ------------------------------------------------------ tiered append ---
+ * Replaces the tiered FA2 batch-prefill module on the append path (run hook
+ * peer/prefill_backend.py:25-42, module peer/flashinfer_peer.py:105-142) and the per-layer
+ * staging of supplier banks (peer/staging.py): remote rows are read in place.
+ * Semantics of FlashInfer's BatchPrefillWithPagedKVCacheWrapper (page_size 1): request b has
+ * qo_indptr[b+1]-qo_indptr[b] query tokens and kv_indptr[b+1]-kv_indptr[b] list entries; with
+ * causal != 0 query token i sees entry j iff j < L_b - q_b (history, any order) or
+ * j - (L_b - q_b) <= i (the query suffix, in order -- the packer's Full list).
+ * dual_append_plan (host): from HOST copies of qo_indptr / kv_indptr, writes the work list
+ * (4 int32 per item: request, kv head, 32-token query tile, cost), costliest first; returns the
+ * item count in *num_work (call with work=NULL to size it).  The work list is then copied to
+ * the device and passed to dual_tiered_append with the DEVICE indptrs.
+ * q/out [sum q, 32, 128] bf16; lse [sum q, 32] fp32 base 2 or NULL; status: device word. */
+int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, int batch, int causal,
+                     int32_t* work_host, int64_t max_work, int64_t* num_work);
+int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                       const void* k_local, const void* v_local, int64_t local_stride_bytes,
+                       int64_t local_capacity,
+                       const void* const* peer_k, const void* const* peer_v, int num_peers,
+                       int64_t peer_stride_bytes, int64_t peer_slots,
+                       const int32_t* qo_indptr, const int32_t* kv_indptr,
+                       const int32_t* unified_indices, int64_t num_indices, int batch, int causal,
+                       double sm_scale, const int32_t* work, int64_t num_work,
+                       void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                       uint32_t* status, int device, void* stream);
+
 /* ------------------------------------------------------ read-order packer ---
  * Replaces Triton _count_remote/_pack_indices + Engine.prepare (peer/backend.py:22-79)
  * and packing.prepare (peer/packing.py:6-36); exact order = peer/layout.py:5-22.
