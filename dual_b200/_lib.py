@@ -9,6 +9,7 @@ elsewhere).
 from __future__ import annotations
 
 import ctypes as C
+import os
 import threading
 from pathlib import Path
 
@@ -95,6 +96,10 @@ class DualError(RuntimeError):
 
 
 def library_path() -> Path:
+    """The in-tree build, or the file named by DUAL_B200_LIBRARY (an alternative build of the same ABI)."""
+    override = os.environ.get("DUAL_B200_LIBRARY")
+    if override:
+        return Path(override)
     return Path(__file__).resolve().parent / "lib" / "libdual_b200.so"
 
 

@@ -5,7 +5,7 @@
 #include <cstring>
 #include <string>
 
-#include "../../include/dual_b200.h"
+#include "dual_b200.h"
 #include "decode.cuh"
 #include "migrate.cuh"
 #include "pack.cuh"

@@ -25,7 +25,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/dual_b200.h"
+#include "dual_b200.h"
 #include "decode.cuh"
 
 namespace dual {

@@ -15,8 +15,10 @@
 // Design (one CTA per work item = request x kv head x 64 query tokens, warp-specialised):
 //   * two query tiles of 32 tokens x 4 GQA heads = 2 x 128 MMA rows share every K/V tile;
 //   * loader warps (2) gather 64-entry K/V tiles (256 B of this kv head per entry, local HBM
-//     or a supplier's HBM through peer loads) with 16-byte cp.async into a 3-stage ring of
-//     128B-swizzled tiles;
+//     or a supplier's HBM through peer loads) with 16-byte cp.async, 16 lanes per entry so every
+//     warp instruction moves whole cache lines, into a 3-stage ring of 128B-swizzled tiles; each
+//     loader arrives on the stage's barrier when its copies land (cp.async.mbarrier.arrive), so
+//     the loaders run up to the ring depth ahead of the tensor core;
 //   * one MMA thread issues S_q = Q_q K^T (tcgen05.mma M128 N64 K16, fp32 in TMEM) for both
 //     query tiles, then O_q += P_q V (M128 N128 K16) once the softmax of tile q is done, so
 //     the tensor core runs QK of one query tile while the other is in softmax;
@@ -42,7 +44,7 @@ constexpr int kRows = kQTok * kGqa;        // 128 MMA rows per query tile
 constexpr int kQTiles = 2;                 // query tiles per CTA
 constexpr int kPairTok = kQTok * kQTiles;  // 64 query tokens per work item
 constexpr int kBN = 64;                    // kv entries per kv tile
-constexpr int kNS = 3;                     // kv ring stages (>= 3: the loaders signal a tile one issue late)
+constexpr int kNS = 3;                     // kv ring stages
 constexpr int kLoadWarps = 2;
 constexpr int kLoadThreads = kLoadWarps * 32;
 constexpr int kSoftmaxWarps = 4 * kQTiles;
@@ -68,6 +70,9 @@ constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ void cp_async_16_zfill(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
                : "memory");
+}
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -149,61 +154,63 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     cp_async_wait<0>();
     fence_proxy_async_smem();
     mbar_arrive(q_full);
-    // kv tiles: thread lt gathers entry j*64 + lt (K and V rows of this kv head)
-    int32_t next_page = 0;
-    if (lt < kv_end) next_page = p.indices[kv0 + lt];
+    // kv tiles: loader warp lw owns entries [32 lw, 32 lw + 32) of each tile; lane l prefetches the
+    // page id of entry 32 lw + l, then 16 lanes cover one entry's 256 B (two full 128 B lines) so each
+    // warp-wide cp.async moves two entries, coalesced.
+    const int lw = lt >> 5;
+    const int half = lane >> 4, chunk = lane & 15;
+    auto page_of = [&](int jj) -> int32_t {  // page id of entry 32 lw + lane of tile jj (0 past the end)
+      const int64_t pos = int64_t(jj) * kBN + 32 * lw + lane;
+      return pos < kv_end ? p.indices[kv0 + pos] : 0;
+    };
+    int32_t page_a = page_of(0), page_b = ntiles > 1 ? page_of(1) : 0;  // two tiles of look-ahead
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int s = j % kNS, f = j / kNS;
-      const int32_t page_raw = next_page;
-      const int64_t pos = int64_t(j) * kBN + lt;
-      if (pos + kBN < kv_end) next_page = p.indices[kv0 + pos + kBN];
+      const int32_t my_page = page_a;
+      page_a = page_b;
+      page_b = j + 2 < ntiles ? page_of(j + 2) : 0;
       if (f > 0 && !wait(kv_empty + s, (f - 1) & 1)) {
         ok = false;
         break;
       }
-      const bool valid = pos < kv_end;
-      const char* ksrc = p.k_local;
-      const char* vsrc = p.v_local;
-      if (valid) {
-        const uint32_t page = static_cast<uint32_t>(page_raw);
-        if (page <= static_cast<uint64_t>(p.local_capacity)) {
-          ksrc = p.k_local + int64_t(page) * p.local_stride;
-          vsrc = p.v_local + int64_t(page) * p.local_stride;
-        } else {
-          const uint32_t gid = page - static_cast<uint32_t>(p.local_capacity) - 1u;
-          const int np = p.num_peers;
-          const uint32_t bank = np > 0 ? gid % uint32_t(np) : 0u;
-          const uint32_t phys = np > 0 ? gid / uint32_t(np) : 0u;
-          if (np <= 0 || int64_t(phys) >= p.peer_slots) {
-            atomicOr(p.status, kStatusBadRemoteSlot);
-          } else {
-            ksrc = p.peer_k[bank] + int64_t(phys) * p.peer_stride;
-            vsrc = p.peer_v[bank] + int64_t(phys) * p.peer_stride;
-          }
-        }
-      }
-      ksrc += h * 256;
-      vsrc += h * 256;
+      const int64_t tile0 = int64_t(j) * kBN;
       unsigned char* sk = smem + kOffKV + s * 2 * kKVBytes;
       unsigned char* sv = sk + kKVBytes;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        cp_async_16_zfill(sk + tc::sw128_offset<kBN>(lt, c), ksrc + c * 16, valid);
-        cp_async_16_zfill(sv + tc::sw128_offset<kBN>(lt, c), vsrc + c * 16, valid);
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int row = 32 * lw + 2 * i + half;  // entry within the tile
+        const uint32_t page = static_cast<uint32_t>(__shfl_sync(0xffffffffu, my_page, 2 * i + half));
+        const bool valid = tile0 + row < kv_end;
+        const char* ksrc = p.k_local;
+        const char* vsrc = p.v_local;
+        if (valid) {
+          if (page <= static_cast<uint64_t>(p.local_capacity)) {
+            ksrc = p.k_local + int64_t(page) * p.local_stride;
+            vsrc = p.v_local + int64_t(page) * p.local_stride;
+          } else {
+            const uint32_t gid = page - static_cast<uint32_t>(p.local_capacity) - 1u;
+            const int np = p.num_peers;
+            const uint32_t bank = np > 0 ? gid % uint32_t(np) : 0u;
+            const uint32_t phys = np > 0 ? gid / uint32_t(np) : 0u;
+            if (np <= 0 || int64_t(phys) >= p.peer_slots) {
+              if (chunk == 0) atomicOr(p.status, kStatusBadRemoteSlot);
+            } else {
+              ksrc = p.peer_k[bank] + int64_t(phys) * p.peer_stride;
+              vsrc = p.peer_v[bank] + int64_t(phys) * p.peer_stride;
+            }
+          }
+        }
+        const int64_t off = h * 256 + chunk * 16;
+        const uint32_t dst = tc::sw128_offset<kBN>(row, chunk);
+        cp_async_16_zfill(sk + dst, ksrc + off, valid);
+        cp_async_16_zfill(sv + dst, vsrc + off, valid);
       }
-      cp_async_commit();
-      if (j > 0) {  // signal the previous tile once its copies are complete (one group stays in flight)
-        cp_async_wait<1>();
-        fence_proxy_async_smem();
-        mbar_arrive(kv_full + (j - 1) % kNS);
-      }
+      // arrive on kv_full when this thread's copies of the tile have landed; keep issuing ahead
+      cp_async_mbar_arrive_noinc(kv_full + s);
     }
-    cp_async_wait<0>();
-    if (ok && ntiles > 0) {
-      fence_proxy_async_smem();
-      mbar_arrive(kv_full + (ntiles - 1) % kNS);
-    }
+    (void)ok;
+    asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == kMmaWarp) {
     // ================================================================ MMA issue (one thread)
     if (lane == 0) {
@@ -231,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           ok = false;
           break;
         }
+        fence_proxy_async_smem();
         tc::fence_after_sync();
         const uint32_t k_base = kv_base + s * 2 * kKVBytes;
         for (int q = 0; q < kQTiles; ++q) {
