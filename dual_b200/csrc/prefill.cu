@@ -16,7 +16,7 @@
 //   * two query tiles of 32 tokens x 4 GQA heads = 2 x 128 MMA rows share every K/V tile;
 //   * loader warps (2) gather 64-entry K/V tiles (256 B of this kv head per entry, local HBM
 //     or a supplier's HBM through peer loads) with 16-byte cp.async, 16 lanes per entry so every
-//     warp instruction moves whole cache lines, into a 3-stage ring of 128B-swizzled tiles; each
+//     warp instruction moves whole cache lines, into a 5-stage ring of 128B-swizzled tiles; each
 //     loader arrives on the stage's barrier when its copies land (cp.async.mbarrier.arrive), so
 //     the loaders run up to the ring depth ahead of the tensor core;
 //   * one MMA thread issues S_q = Q_q K^T (tcgen05.mma M128 N64 K16, fp32 in TMEM) for both
@@ -25,8 +25,9 @@
 //   * one softmax warpgroup per query tile (thread = TMEM lane = row): mask only on tiles that
 //     cross the causal diagonal or the end, scale + exp2 as one FMA + one MUFU per score,
 //     lazy rescaling of O (the reference max moves only when it grows by more than 2^8),
-//     P written as a bf16 pair hi + lo (P's bf16 rounding would otherwise move short-row
-//     outputs by ~4e-3 under cancellation); epilogue O / rowsum -> bf16, LSE = m + log2 rowsum.
+//     P written to tensor memory (tcgen05.st) as a bf16 pair hi + lo (P's bf16 rounding would
+//     otherwise move short-row outputs by ~4e-3 under cancellation) and consumed from there by
+//     the PV MMA; epilogue O / rowsum -> bf16, LSE = m + log2 rowsum.
 // All waits are bounded; a timed-out wait records DUAL_STATUS_WAIT_TIMEOUT and every role
 // unwinds (no thread is left at a barrier the others skipped).
 #include <algorithm>
@@ -44,7 +45,7 @@ constexpr int kRows = kQTok * kGqa;        // 128 MMA rows per query tile
 constexpr int kQTiles = 2;                 // query tiles per CTA
 constexpr int kPairTok = kQTok * kQTiles;  // 64 query tokens per work item
 constexpr int kBN = 64;                    // kv entries per kv tile
-constexpr int kNS = 3;                     // kv ring stages
+constexpr int kNS = 5;                     // kv ring stages
 constexpr int kLoadWarps = 2;
 constexpr int kLoadThreads = kLoadWarps * 32;
 constexpr int kSoftmaxWarps = 4 * kQTiles;
@@ -54,18 +55,18 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: p stays <= 256 between
 
 constexpr int kQBytes = kRows * 256;       // 32 KB: [128 rows x 128 dims] bf16
 constexpr int kKVBytes = kBN * 256;        // 16 KB: [64 entries x 128 dims] bf16
-constexpr int kPBytes = kRows * kBN * 2;   // 16 KB: [128 rows x 64 entries] bf16
-// smem: Q0 Q1 | (K, V) x 3 stages | (P_hi, P_lo) x 2 query tiles | barriers
+// smem: Q0 Q1 | (K, V) x kNS stages | barriers   (P lives in tensor memory)
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kQTiles * kQBytes;
-constexpr int kOffP = kOffKV + kNS * 2 * kKVBytes;
-constexpr int kOffBar = kOffP + kQTiles * 2 * kPBytes;
+constexpr int kOffBar = kOffKV + kNS * 2 * kKVBytes;
 constexpr int kNumBars = 2 * kNS + 3 * kQTiles + 1;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // TMEM columns: S0 [0,64) S1 [64,128) O0 [128,256) O1 [256,384)
+//               P0 hi [384,416) lo [416,448)  P1 hi [448,480) lo [480,512)   (bf16 pairs per column)
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColP = 384;
 
 __device__ __forceinline__ void cp_async_16_zfill(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
@@ -218,16 +219,15 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, 0, 1);
       const uint32_t q_base = smem_addr(smem + kOffQ);
       const uint32_t kv_base = smem_addr(smem + kOffKV);
-      const uint32_t p_base = smem_addr(smem + kOffP);
       auto issue_pv = [&](int q, int jj) {
         const uint32_t v_base = kv_base + (jj % kNS) * 2 * kKVBytes + kKVBytes;
-        const uint32_t ph = p_base + q * 2 * kPBytes, pl = ph + kPBytes;
+        const uint32_t ph = tmem + kColP + q * 64, pl = ph + 32;  // 16 bf16 of K = 8 columns per MMA
         const uint32_t tO = tmem + 128 + q * 128;
 #pragma unroll
         for (int kb = 0; kb < kBN / 16; ++kb) {
           const uint64_t vdesc = tc::smem_desc_sw128(v_base + kb * 2048, kBN * 128, 1024);
-          tc::mma_bf16(tO, tc::smem_desc_sw128(ph + kb * 32, 16, 1024), vdesc, kIdescPV, (jj > 0 || kb > 0) ? 1u : 0u);
-          tc::mma_bf16(tO, tc::smem_desc_sw128(pl + kb * 32, 16, 1024), vdesc, kIdescPV, 1u);
+          tc::mma_bf16_ts(tO, ph + kb * 8, vdesc, kIdescPV, (jj > 0 || kb > 0) ? 1u : 0u);
+          tc::mma_bf16_ts(tO, pl + kb * 8, vdesc, kIdescPV, 1u);
         }
         tc::commit(o_done + q);
       };
@@ -282,8 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     const int64_t tok = tok_first + r / kGqa;
     const bool row_valid = tok < t_end;
     const float scale = p.scale_log2;
-    unsigned char* sPh = smem + kOffP + q * 2 * kPBytes;
-    unsigned char* sPl = sPh + kPBytes;
+    const uint32_t tPh = tmem + kColP + q * 64 + lane_base, tPl = tPh + 32;
     float m_used = -INFINITY, d_sum = 0.f;  // m_used in the scaled (log2) domain
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
@@ -330,23 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       tc::fence_after_sync();
       const float neg_m = -m_used;
       float rs = 0.f;
+      uint32_t hi[kBN / 2], lo[kBN / 2];
 #pragma unroll
-      for (int c = 0; c < kBN; c += 8) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = fast_exp2(fmaf(x[c + e], scale, neg_m));
-          rs += pv[e];
-        }
-        uint4 hi, lo;
-        split_bf16x2(pv[0], pv[1], hi.x, lo.x);
-        split_bf16x2(pv[2], pv[3], hi.y, lo.y);
-        split_bf16x2(pv[4], pv[5], hi.z, lo.z);
-        split_bf16x2(pv[6], pv[7], hi.w, lo.w);
-        const uint32_t off = tc::sw128_offset<kRows>(r, c >> 3);
-        *reinterpret_cast<uint4*>(sPh + off) = hi;
-        *reinterpret_cast<uint4*>(sPl + off) = lo;
+      for (int c = 0; c < kBN; c += 2) {
+        const float p0 = fast_exp2(fmaf(x[c], scale, neg_m));
+        const float p1 = fast_exp2(fmaf(x[c + 1], scale, neg_m));
+        rs += p0 + p1;
+        split_bf16x2(p0, p1, hi[c / 2], lo[c / 2]);
       }
+      tc::st32u(tPh, hi);
+      tc::st32u(tPl, lo);
       d_sum = d_sum * alpha + rs;
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
         const float a = rescale ? alpha : 1.f;
@@ -361,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         }
         tc::wait_st();
       }
-      fence_proxy_async_smem();  // P (generic-proxy stores) -> tensor core
+      tc::wait_st();  // P (and any rescaled O) in tensor memory before the MMA thread reads them
       tc::fence_before_sync();
       mbar_arrive(p_full + q);
     }
