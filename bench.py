@@ -624,6 +624,7 @@ APPEND = {
     # name: (requests, qmin, qmax (log-uniform), Pmin, Pmax (uniform), remote/local, suppliers)
     "config4": (32, 128, 2048, 4096, 32768, 0.1797, 3),
     "append-small": (4, 128, 512, 1024, 4096, 0.1797, 3),
+    "append-mid": (8, 128, 2048, 4096, 32768, 0.1797, 3),  # the profiling case: ~0.7 GB on the device
 }
 
 
