@@ -11,23 +11,30 @@
 // entry j iff j < L_b - q_b (the fully visible, possibly re-ordered history) or
 // j - (L_b - q_b) <= i (the query suffix, kept in order by the packer); without
 // `causal` every entry is visible.  Output bf16 [sum q, 32, 128], LSE base 2.
+// Arithmetic follows the reference's append kernel
+// (final/vendor/nvlink_prefill/launch_20261031_r5/code/paged_prefill.py:36-57): scores
+// scaled into the log2 domain, online softmax in fp32, and P entering P @ V as a bf16
+// high part plus the bf16 residual p - high (PROB_RESIDUAL, on by default there).
 //
 // Design (one CTA per work item = request x kv head x 64 query tokens, warp-specialised):
 //   * two query tiles of 32 tokens x 4 GQA heads = 2 x 128 MMA rows share every K/V tile;
-//   * loader warps (2) gather 64-entry K/V tiles (256 B of this kv head per entry, local HBM
-//     or a supplier's HBM through peer loads) with 16-byte cp.async, 16 lanes per entry so every
-//     warp instruction moves whole cache lines, into a 5-stage ring of 128B-swizzled tiles; each
-//     loader arrives on the stage's barrier when its copies land (cp.async.mbarrier.arrive), so
-//     the loaders run up to the ring depth ahead of the tensor core;
-//   * one MMA thread issues S_q = Q_q K^T (tcgen05.mma M128 N64 K16, fp32 in TMEM) for both
-//     query tiles, then O_q += P_q V (M128 N128 K16) once the softmax of tile q is done, so
-//     the tensor core runs QK of one query tile while the other is in softmax;
+//     kv tiles are 128 entries: a tcgen05.mma of K = 16 costs the same ~76 cycles for any
+//     N <= 128, so N = 128 score tiles halve the QK^T instructions per key against N = 64;
+//   * loader warps (2) gather K and V tiles (128 entries x 256 B of this kv head, local HBM or
+//     a supplier's HBM through peer loads) with 16-byte cp.async, 16 lanes per entry so every
+//     warp instruction moves whole cache lines, into a 5-slot ring of 32 KB 128B-swizzled
+//     tiles filled in the order K0 V0 K1 V1 ...; each loader arrives on the slot's barrier when
+//     its copies land (cp.async.mbarrier.arrive), so loads run ahead of the tensor core;
+//   * one MMA thread issues, per kv tile j and query tile q: O_q += P_q(j-1) V(j-1) (hi and lo,
+//     A operand read from tensor memory) and then S_q = Q_q K(j)^T into the same TMEM columns
+//     (tcgen05.mma instructions of one thread execute in issue order, so the PV reads P before
+//     the next QK overwrites it); one commit per query tile and kv tile tells the softmax both
+//     that S_q(j) is ready and that O_q is quiescent;
 //   * one softmax warpgroup per query tile (thread = TMEM lane = row): mask only on tiles that
-//     cross the causal diagonal or the end, scale + exp2 as one FMA + one MUFU per score,
-//     lazy rescaling of O (the reference max moves only when it grows by more than 2^8),
-//     P written to tensor memory (tcgen05.st) as a bf16 pair hi + lo (P's bf16 rounding would
-//     otherwise move short-row outputs by ~4e-3 under cancellation) and consumed from there by
-//     the PV MMA; epilogue O / rowsum -> bf16, LSE = m + log2 rowsum.
+//     cross the causal diagonal or the end, scale + exp2 as one FMA + one MUFU per score, lazy
+//     rescaling of O in place (the reference max moves only when it grows by more than 2^8),
+//     P written over its own S columns as bf16 hi/lo pairs (tcgen05.st); epilogue
+//     O / rowsum -> bf16, LSE = m + log2 rowsum.
 // All waits are bounded; a timed-out wait records DUAL_STATUS_WAIT_TIMEOUT and every role
 // unwinds (no thread is left at a barrier the others skipped).
 #include <algorithm>
@@ -44,8 +51,8 @@ constexpr int kQTok = 32;                  // query tokens per query tile
 constexpr int kRows = kQTok * kGqa;        // 128 MMA rows per query tile
 constexpr int kQTiles = 2;                 // query tiles per CTA
 constexpr int kPairTok = kQTok * kQTiles;  // 64 query tokens per work item
-constexpr int kBN = 64;                    // kv entries per kv tile
-constexpr int kNS = 5;                     // kv ring stages
+constexpr int kBN = 128;                   // kv entries per kv tile
+constexpr int kSlots = 5;                  // ring slots, each one K or one V tile
 constexpr int kLoadWarps = 2;
 constexpr int kLoadThreads = kLoadWarps * 32;
 constexpr int kSoftmaxWarps = 4 * kQTiles;
@@ -54,19 +61,20 @@ constexpr int kThreads = (kMmaWarp + 1) * 32;          // 352
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: p stays <= 256 between rescales
 
 constexpr int kQBytes = kRows * 256;       // 32 KB: [128 rows x 128 dims] bf16
-constexpr int kKVBytes = kBN * 256;        // 16 KB: [64 entries x 128 dims] bf16
-// smem: Q0 Q1 | (K, V) x kNS stages | barriers   (P lives in tensor memory)
+constexpr int kSlotBytes = kBN * 256;      // 32 KB: [128 entries x 128 dims] bf16
+// smem: Q0 Q1 | kSlots x (K or V tile) | barriers
 constexpr int kOffQ = 0;
-constexpr int kOffKV = kQTiles * kQBytes;
-constexpr int kOffBar = kOffKV + kNS * 2 * kKVBytes;
-constexpr int kNumBars = 2 * kNS + 3 * kQTiles + 1;
+constexpr int kOffSlot = kQTiles * kQBytes;
+constexpr int kOffBar = kOffSlot + kSlots * kSlotBytes;
+constexpr int kNumBars = 2 * kSlots + 3 * kQTiles + 1;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-// TMEM columns: S0 [0,64) S1 [64,128) O0 [128,256) O1 [256,384)
-//               P0 hi [384,416) lo [416,448)  P1 hi [448,480) lo [480,512)   (bf16 pairs per column)
+// TMEM columns: S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
+// P of kv chunk c (entries 32c..32c+31) lives over S columns [32c, 32c+32): bf16 pairs, hi in the
+// first 16 columns, lo in the last 16, so each chunk's P only overwrites scores already read.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColP = 384;
+constexpr uint32_t kColO = 256;
 
 __device__ __forceinline__ void cp_async_16_zfill(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
@@ -84,12 +92,12 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* kv_full = bars;                      // [kNS]  count kLoadThreads
-  uint64_t* kv_empty = bars + kNS;               // [kNS]  count 1 (tcgen05.commit)
-  uint64_t* s_full = bars + 2 * kNS;             // [2]    count 1 (tcgen05.commit)
-  uint64_t* p_full = s_full + kQTiles;           // [2]    count 128 (softmax warpgroup)
-  uint64_t* o_done = p_full + kQTiles;           // [2]    count 1 (tcgen05.commit)
-  uint64_t* q_full = o_done + kQTiles;           // [1]    count kLoadThreads
+  uint64_t* slot_full = bars;                    // [kSlots] count kLoadThreads
+  uint64_t* slot_empty = bars + kSlots;          // [kSlots] count 1 (tcgen05.commit)
+  uint64_t* s_full = bars + 2 * kSlots;          // [2]      count 1 (tcgen05.commit)
+  uint64_t* p_full = s_full + kQTiles;           // [2]      count 128 (softmax warpgroup)
+  uint64_t* o_done = p_full + kQTiles;           // [2]      count 1 (tcgen05.commit, last PV)
+  uint64_t* q_full = o_done + kQTiles;           // [1]      count kLoadThreads
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars) + 1;
 
@@ -109,10 +117,19 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
   const int64_t kv_end = p.causal ? min(L, prefix + t_end) : L;
   const int ntiles = int((kv_end + kBN - 1) / kBN);
 
+  // supplier bank pointers in shared memory: the loaders index them by bank at run time, and
+  // indexing the kernel's parameter block instead would make every parameter a memory operand
+  // that each asm statement with a memory clobber forces the compiler to reload
+  __shared__ const char* s_peer[2][kMaxPeers];
   if (tid == 0) {
-    for (int s = 0; s < kNS; ++s) {
-      mbar_init(kv_full + s, kLoadThreads);
-      mbar_init(kv_empty + s, 1);
+#pragma unroll
+    for (int i = 0; i < kMaxPeers; ++i) {  // constant indices: plain parameter loads
+      s_peer[0][i] = p.peer_k[i];
+      s_peer[1][i] = p.peer_v[i];
+    }
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(slot_full + s, kLoadThreads);
+      mbar_init(slot_empty + s, 1);
     }
     for (int q = 0; q < kQTiles; ++q) {
       mbar_init(s_full + q, 1);
@@ -155,60 +172,89 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     cp_async_wait<0>();
     fence_proxy_async_smem();
     mbar_arrive(q_full);
-    // kv tiles: loader warp lw owns entries [32 lw, 32 lw + 32) of each tile; lane l prefetches the
-    // page id of entry 32 lw + l, then 16 lanes cover one entry's 256 B (two full 128 B lines) so each
-    // warp-wide cp.async moves two entries, coalesced.
+    // kv tiles: loader warp lw owns entries [64 lw, 64 lw + 64) of each tile.  Lane l resolves the
+    // page ids of entries 64 lw + l and 64 lw + 32 + l into K and V row pointers one tile ahead of
+    // use (the ids themselves are loaded two tiles ahead); the copy loop then only shuffles a
+    // pointer: 16 lanes cover one entry's 256 B (two full 128 B lines), so each warp-wide cp.async
+    // moves two entries, coalesced.  Resolving inside the copy loop (the remote branch with its
+    // division and status update once per copy) made the loop four times slower.
     const int lw = lt >> 5;
     const int half = lane >> 4, chunk = lane & 15;
-    auto page_of = [&](int jj) -> int32_t {  // page id of entry 32 lw + lane of tile jj (0 past the end)
-      const int64_t pos = int64_t(jj) * kBN + 32 * lw + lane;
-      return pos < kv_end ? p.indices[kv0 + pos] : 0;
+    const int32_t* const indices = p.indices + kv0;
+    const char* const k_local = p.k_local;
+    const char* const v_local = p.v_local;
+    const int64_t local_stride = p.local_stride, peer_stride = p.peer_stride, peer_slots = p.peer_slots;
+    const uint32_t capacity = static_cast<uint32_t>(p.local_capacity);
+    const uint32_t np = static_cast<uint32_t>(max(p.num_peers, 0));
+    unsigned* const status = p.status;
+    const int64_t off = h * 256 + chunk * 16;
+    auto page_of = [&](int jj, int sub) -> int32_t {  // page id of entry 64 lw + 32 sub + lane (0 past the end)
+      const int64_t pos = int64_t(jj) * kBN + 64 * lw + 32 * sub + lane;
+      return pos < kv_end ? __ldg(indices + pos) : 0;
     };
-    int32_t page_a = page_of(0), page_b = ntiles > 1 ? page_of(1) : 0;  // two tiles of look-ahead
-    bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int s = j % kNS, f = j / kNS;
-      const int32_t my_page = page_a;
-      page_a = page_b;
-      page_b = j + 2 < ntiles ? page_of(j + 2) : 0;
-      if (f > 0 && !wait(kv_empty + s, (f - 1) & 1)) {
-        ok = false;
-        break;
-      }
-      const int64_t tile0 = int64_t(j) * kBN;
-      unsigned char* sk = smem + kOffKV + s * 2 * kKVBytes;
-      unsigned char* sv = sk + kKVBytes;
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const int row = 32 * lw + 2 * i + half;  // entry within the tile
-        const uint32_t page = static_cast<uint32_t>(__shfl_sync(0xffffffffu, my_page, 2 * i + half));
-        const bool valid = tile0 + row < kv_end;
-        const char* ksrc = p.k_local;
-        const char* vsrc = p.v_local;
-        if (valid) {
-          if (page <= static_cast<uint64_t>(p.local_capacity)) {
-            ksrc = p.k_local + int64_t(page) * p.local_stride;
-            vsrc = p.v_local + int64_t(page) * p.local_stride;
-          } else {
-            const uint32_t gid = page - static_cast<uint32_t>(p.local_capacity) - 1u;
-            const int np = p.num_peers;
-            const uint32_t bank = np > 0 ? gid % uint32_t(np) : 0u;
-            const uint32_t phys = np > 0 ? gid / uint32_t(np) : 0u;
-            if (np <= 0 || int64_t(phys) >= p.peer_slots) {
-              if (chunk == 0) atomicOr(p.status, kStatusBadRemoteSlot);
-            } else {
-              ksrc = p.peer_k[bank] + int64_t(phys) * p.peer_stride;
-              vsrc = p.peer_v[bank] + int64_t(phys) * p.peer_stride;
-            }
-          }
+    // page id -> row pointers of both planes (page 0 of the local pool for a bad remote id, which is
+    // recorded in the status word)
+    auto resolve = [&](int32_t page_id, const char*& kp, const char*& vp) {
+      const uint32_t page = static_cast<uint32_t>(page_id);
+      if (page <= capacity) {
+        kp = k_local + int64_t(page) * local_stride;
+        vp = v_local + int64_t(page) * local_stride;
+      } else {
+        const uint32_t gid = page - capacity - 1u;
+        const uint32_t bank = np > 0 ? gid % np : 0u;
+        const uint32_t phys = np > 0 ? gid / np : 0u;
+        if (np == 0 || int64_t(phys) >= peer_slots) {
+          atomicOr(status, kStatusBadRemoteSlot);
+          kp = k_local;
+          vp = v_local;
+        } else {
+          kp = s_peer[0][bank] + int64_t(phys) * peer_stride;
+          vp = s_peer[1][bank] + int64_t(phys) * peer_stride;
         }
-        const int64_t off = h * 256 + chunk * 16;
-        const uint32_t dst = tc::sw128_offset<kBN>(row, chunk);
-        cp_async_16_zfill(sk + dst, ksrc + off, valid);
-        cp_async_16_zfill(sv + dst, vsrc + off, valid);
       }
-      // arrive on kv_full when this thread's copies of the tile have landed; keep issuing ahead
-      cp_async_mbar_arrive_noinc(kv_full + s);
+    };
+    const char *k0, *k1, *v0, *v1;  // row pointers of this lane's two entries, current tile
+    resolve(page_of(0, 0), k0, v0);
+    resolve(page_of(0, 1), k1, v1);
+    int32_t next0 = ntiles > 1 ? page_of(1, 0) : 0, next1 = ntiles > 1 ? page_of(1, 1) : 0;
+    auto shfl_ptr = [](const char* ptr, int src_lane) {
+      const unsigned long long v = reinterpret_cast<unsigned long long>(ptr);
+      const uint32_t lo = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v), src_lane);
+      const uint32_t hi = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), src_lane);
+      return reinterpret_cast<const char*>((static_cast<unsigned long long>(hi) << 32) | lo);
+    };
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int32_t after0 = j + 2 < ntiles ? page_of(j + 2, 0) : 0;  // lands while this tile issues
+      const int32_t after1 = j + 2 < ntiles ? page_of(j + 2, 1) : 0;
+      const int64_t tile0 = int64_t(j) * kBN;
+#pragma unroll 1
+      for (int plane = 0; plane < 2; ++plane) {  // K then V of tile j
+        const int u = 2 * j + plane, s = u % kSlots, f = u / kSlots;
+        if (f > 0 && !wait(slot_empty + s, uint32_t(f - 1) & 1u)) {
+          ok = false;
+          break;
+        }
+        const char* const r0 = plane == 0 ? k0 : v0;
+        const char* const r1 = plane == 0 ? k1 : v1;
+        unsigned char* dst_tile = smem + kOffSlot + s * kSlotBytes;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) {
+          const int rr = 2 * i + half;  // entry within this warp's 64
+          const int row = 64 * lw + rr;
+          const char* src = shfl_ptr(i < 16 ? r0 : r1, rr & 31);
+          const bool valid = tile0 + row < kv_end;
+          cp_async_16_zfill(dst_tile + tc::sw128_offset<kBN>(row, chunk), src + off, valid);
+        }
+        // arrive on the slot's barrier when this thread's copies have landed; keep issuing ahead
+        cp_async_mbar_arrive_noinc(slot_full + s);
+      }
+      if (j + 1 < ntiles) {
+        resolve(next0, k0, v0);
+        resolve(next1, k1, v1);
+      }
+      next0 = after0;
+      next1 = after1;
     }
     (void)ok;
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -218,36 +264,39 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       constexpr uint32_t kIdescQK = tc::idesc_bf16_f32(128, kBN, 0, 0);
       constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, 0, 1);
       const uint32_t q_base = smem_addr(smem + kOffQ);
-      const uint32_t kv_base = smem_addr(smem + kOffKV);
+      const uint32_t slot_base = smem_addr(smem + kOffSlot);
+      auto slot_addr = [&](int u) { return slot_base + uint32_t(u % kSlots) * kSlotBytes; };
+      auto slot_wait = [&](int u) { return wait(slot_full + u % kSlots, uint32_t(u / kSlots) & 1u); };
+      // O_q (+)= P_q V(jj): 8 k-steps of 16 entries, each a hi and a lo MMA with A from TMEM
       auto issue_pv = [&](int q, int jj) {
-        const uint32_t v_base = kv_base + (jj % kNS) * 2 * kKVBytes + kKVBytes;
-        const uint32_t ph = tmem + kColP + q * 64, pl = ph + 32;  // 16 bf16 of K = 8 columns per MMA
-        const uint32_t tO = tmem + 128 + q * 128;
+        const uint32_t v_base = slot_addr(2 * jj + 1);
+        const uint32_t tP = tmem + q * kBN;
+        const uint32_t tO = tmem + kColO + q * 128;
 #pragma unroll
         for (int kb = 0; kb < kBN / 16; ++kb) {
           const uint64_t vdesc = tc::smem_desc_sw128(v_base + kb * 2048, kBN * 128, 1024);
-          tc::mma_bf16_ts(tO, ph + kb * 8, vdesc, kIdescPV, (jj > 0 || kb > 0) ? 1u : 0u);
-          tc::mma_bf16_ts(tO, pl + kb * 8, vdesc, kIdescPV, 1u);
+          const uint32_t ph = tP + 32 * (kb >> 1) + 8 * (kb & 1);
+          tc::mma_bf16_ts(tO, ph, vdesc, kIdescPV, (jj > 0 || kb > 0) ? 1u : 0u);
+          tc::mma_bf16_ts(tO, ph + 16, vdesc, kIdescPV, 1u);
         }
-        tc::commit(o_done + q);
       };
       bool ok = wait(q_full, 0);
       for (int j = 0; j < ntiles && ok; ++j) {
-        const int s = j % kNS;
-        if (!wait(kv_full + s, uint32_t(j / kNS) & 1u)) {
+        if (!slot_wait(2 * j) || (j > 0 && !slot_wait(2 * j - 1))) {  // K(j), V(j-1)
           ok = false;
           break;
         }
         fence_proxy_async_smem();
         tc::fence_after_sync();
-        const uint32_t k_base = kv_base + s * 2 * kKVBytes;
+        const uint32_t k_base = slot_addr(2 * j);
         for (int q = 0; q < kQTiles; ++q) {
-          if (j > 0) {  // softmax of (q, j-1) done: S_q is free and P_q(j-1) is ready
+          if (j > 0) {  // softmax of (q, j-1) done: P_q(j-1) is in TMEM
             if (!wait(p_full + q, uint32_t(j - 1) & 1u)) {
               ok = false;
               break;
             }
             tc::fence_after_sync();
+            issue_pv(q, j - 1);
           }
           const uint32_t qb = q_base + q * kQBytes;
 #pragma unroll
@@ -257,11 +306,13 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
             tc::mma_bf16(tmem + q * kBN, tc::smem_desc_sw128(qb + off_q, 16, 1024),
                          tc::smem_desc_sw128(k_base + off_k, 16, 1024), kIdescQK, kb > 0);
           }
-          tc::commit(s_full + q);
-          if (j > 0) issue_pv(q, j - 1);
+          tc::commit(s_full + q);  // S_q(j) written, PV_q(j-1) done
         }
-        if (ok && j > 0) tc::commit(kv_empty + (j - 1) % kNS);  // frees that stage once PV(., j-1) completes
+        if (!ok) break;
+        tc::commit(slot_empty + (2 * j) % kSlots);                 // K(j) consumed by both QKs
+        if (j > 0) tc::commit(slot_empty + (2 * j - 1) % kSlots);  // V(j-1) consumed by both PVs
       }
+      if (ok && ntiles > 0) ok = slot_wait(2 * ntiles - 1);
       for (int q = 0; q < kQTiles && ok && ntiles > 0; ++q) {
         if (!wait(p_full + q, uint32_t(ntiles - 1) & 1u)) {
           ok = false;
@@ -269,6 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         }
         tc::fence_after_sync();
         issue_pv(q, ntiles - 1);
+        tc::commit(o_done + q);
       }
     }
   } else {
@@ -277,12 +329,12 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     const int r = tid - q * kRows;          // row = TMEM lane
     const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + q * kBN + lane_base;
-    const uint32_t tO = tmem + 128 + q * 128 + lane_base;
+    const uint32_t tO = tmem + kColO + q * 128 + lane_base;
     const int64_t tok_first = t_begin + q * kQTok;           // first token of this query tile
     const int64_t tok = tok_first + r / kGqa;
     const bool row_valid = tok < t_end;
     const float scale = p.scale_log2;
-    const uint32_t tPh = tmem + kColP + q * 64 + lane_base, tPl = tPh + 32;
+    const bool causal = p.causal != 0;
     float m_used = -INFINITY, d_sum = 0.f;  // m_used in the scaled (log2) domain
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
@@ -292,28 +344,38 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         break;
       }
       tc::fence_after_sync();
-      float x[kBN];
-      tc::ld32(tS, x);
-      tc::ld32(tS + 32, x + 32);
-      tc::wait_ld();
       const int64_t base_pos = int64_t(j) * kBN;
       // a tile needs a mask only if it reaches past the end or across this query tile's diagonal
-      const bool needs_mask =
-          base_pos + kBN > kv_end || (p.causal && base_pos + kBN > prefix + tok_first + 1) || !row_valid;
-      float tmax = -INFINITY;
-      if (__any_sync(0xffffffffu, needs_mask)) {
-        const int64_t lim = (row_valid && p.causal) ? min(kv_end, prefix + tok + 1) : kv_end;
-        const int vis = int(max(int64_t(0), min(int64_t(kBN), lim - base_pos)));
+      const bool needs_mask = __any_sync(
+          0xffffffffu,
+          base_pos + kBN > kv_end || (causal && base_pos + kBN > prefix + tok_first + 1) || !row_valid);
+      const int64_t lim = (row_valid && causal) ? min(kv_end, prefix + tok + 1) : kv_end;
+      const int vis = int(max(int64_t(0), min(int64_t(kBN), lim - base_pos)));  // visible entries
+      // scores in two halves of 64 columns (64 live registers): max over both, the second half
+      // stays live for the exponentials and the first half is read again afterwards
+      float x[64];
+      auto load_half = [&](int c0) {
+        tc::ld32(tS + c0, x);
+        tc::ld32(tS + c0 + 32, x + 32);
+        tc::wait_ld();
+        if (needs_mask) {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          x[c] = c < vis ? x[c] : -INFINITY;
-          tmax = fmaxf(tmax, x[c]);
+          for (int c = 0; c < 64; ++c) x[c] = c0 + c < vis ? x[c] : -INFINITY;
         }
-      } else {
+      };
+      auto half_max = [&]() {
+        float m4[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) tmax = fmaxf(tmax, x[c]);
-      }
-      tmax *= scale;
+        for (int c = 4; c < 64; c += 4) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) m4[e] = fmaxf(m4[e], x[c + e]);
+        }
+        return fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      };
+      load_half(0);
+      float tmax = half_max();
+      load_half(64);
+      tmax = fmaxf(tmax, half_max()) * scale;
       float alpha = 1.f;
       bool rescale = false;
       if (tmax > m_used + kRescaleThreshold) {
@@ -321,28 +383,10 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         m_used = tmax;
         rescale = true;
       }
-      // P_q and O_q are still in use by PV(q, j-1) until o_done
-      if (j > 0 && !__all_sync(0xffffffffu, wait(o_done + q, uint32_t(j - 1) & 1u))) {
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      const float neg_m = -m_used;
-      float rs = 0.f;
-      uint32_t hi[kBN / 2], lo[kBN / 2];
-#pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float p0 = fast_exp2(fmaf(x[c], scale, neg_m));
-        const float p1 = fast_exp2(fmaf(x[c + 1], scale, neg_m));
-        rs += p0 + p1;
-        split_bf16x2(p0, p1, hi[c / 2], lo[c / 2]);
-      }
-      tc::st32u(tPh, hi);
-      tc::st32u(tPl, lo);
-      d_sum = d_sum * alpha + rs;
+      // O_q is quiescent here: PV_q(j-1) completed before s_full(j), PV_q(j) waits for p_full(j)
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
         const float a = rescale ? alpha : 1.f;
-#pragma unroll
+#pragma unroll 1
         for (int c0 = 0; c0 < 128; c0 += 32) {
           float o[32];
           tc::ld32(tO + c0, o);
@@ -351,14 +395,34 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           for (int e = 0; e < 32; ++e) o[e] *= a;
           tc::st32(tO + c0, o);
         }
-        tc::wait_st();
       }
+      const float neg_m = -m_used;
+      float rs = 0.f;
+      // P of the live half (entries 64..127), then of the first half, each over its own columns
+      auto emit_half = [&](int c0) {
+#pragma unroll
+        for (int cc = 0; cc < 64; cc += 32) {
+          uint32_t v[32];  // [0,16) hi pairs, [16,32) lo pairs of entries c0 + cc .. + 31
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = fast_exp2(fmaf(x[cc + 2 * i], scale, neg_m));
+            const float p1 = fast_exp2(fmaf(x[cc + 2 * i + 1], scale, neg_m));
+            rs += p0 + p1;
+            split_bf16x2(p0, p1, v[i], v[16 + i]);
+          }
+          tc::st32u(tS + c0 + cc, v);
+        }
+      };
+      emit_half(64);
+      load_half(0);
+      emit_half(0);
+      d_sum = d_sum * alpha + rs;
       tc::wait_st();  // P (and any rescaled O) in tensor memory before the MMA thread reads them
       tc::fence_before_sync();
       mbar_arrive(p_full + q);
     }
     // ---- epilogue: after the last PV of this query tile
-    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, wait(o_done + q, uint32_t(ntiles - 1) & 1u));
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, wait(o_done + q, 0));
     tc::fence_after_sync();
     if (ok) {
       const float inv = d_sum > 0.f ? 1.f / d_sum : 0.f;
@@ -391,8 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     if (*abort_flag) {
       // an aborted CTA may still have MMAs in flight: give them a bounded chance before TMEM goes
       for (int q = 0; q < kQTiles; ++q) {
-        mbar_wait_bounded(o_done + q, 0);
-        mbar_wait_bounded(o_done + q, 1);
+        mbar_wait_bounded(s_full + q, 0);
+        mbar_wait_bounded(s_full + q, 1);
       }
     }
     tc::dealloc(tmem, kTmemCols);
