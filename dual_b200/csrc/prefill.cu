@@ -66,7 +66,7 @@ constexpr int kSlotBytes = kBN * 256;      // 32 KB: [128 entries x 128 dims] bf
 constexpr int kOffQ = 0;
 constexpr int kOffSlot = kQTiles * kQBytes;
 constexpr int kOffBar = kOffSlot + kSlots * kSlotBytes;
-constexpr int kNumBars = 2 * kSlots + 3 * kQTiles + 1;
+constexpr int kNumBars = 2 * kSlots + 4 * kQTiles + 1;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
@@ -95,8 +95,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
   uint64_t* slot_full = bars;                    // [kSlots] count kLoadThreads
   uint64_t* slot_empty = bars + kSlots;          // [kSlots] count 1 (tcgen05.commit)
   uint64_t* s_full = bars + 2 * kSlots;          // [2]      count 1 (tcgen05.commit)
-  uint64_t* p_full = s_full + kQTiles;           // [2]      count 128 (softmax warpgroup)
-  uint64_t* o_done = p_full + kQTiles;           // [2]      count 1 (tcgen05.commit, last PV)
+  uint64_t* p_part = s_full + kQTiles;           // [2 x 2]  count 128: P of entries 64..127, then 0..63
+  uint64_t* o_done = p_part + 2 * kQTiles;       // [2]      count 1 (tcgen05.commit, last PV)
   uint64_t* q_full = o_done + kQTiles;           // [1]      count kLoadThreads
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars) + 1;
@@ -133,7 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     }
     for (int q = 0; q < kQTiles; ++q) {
       mbar_init(s_full + q, 1);
-      mbar_init(p_full + q, kRows);
+      mbar_init(p_part + 2 * q, kRows);
+      mbar_init(p_part + 2 * q + 1, kRows);
       mbar_init(o_done + q, 1);
     }
     mbar_init(q_full, kLoadThreads);
@@ -146,7 +147,10 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  // fast path first: under the tensor core's operand traffic every shared-memory access of a
+  // waiting thread is slow, so the abort flag is read only when the phase is not complete yet
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (mbar_wait_bounded(bar, parity)) return true;
     *abort_flag = 1;
@@ -260,6 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == kMmaWarp) {
     // ================================================================ MMA issue (one thread)
+    // Query tiles alternate (PV_0 QK_0, PV_1 QK_1), so the tensor core works on one tile while the
+    // other is in softmax; within a tile PV_q(j-1) is issued before QK_q(j), which overwrites P_q.
     if (lane == 0) {
       constexpr uint32_t kIdescQK = tc::idesc_bf16_f32(128, kBN, 0, 0);
       constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, 0, 1);
@@ -267,36 +273,52 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       const uint32_t slot_base = smem_addr(smem + kOffSlot);
       auto slot_addr = [&](int u) { return slot_base + uint32_t(u % kSlots) * kSlotBytes; };
       auto slot_wait = [&](int u) { return wait(slot_full + u % kSlots, uint32_t(u / kSlots) & 1u); };
-      // O_q (+)= P_q V(jj): 8 k-steps of 16 entries, each a hi and a lo MMA with A from TMEM
-      auto issue_pv = [&](int q, int jj) {
+      // O_q (+)= P_q V(jj), k-steps of 16 entries, each a hi and a lo MMA with A from TMEM; part 0 is
+      // entries 64..127 (k-steps 4..7, the first P the softmax writes), part 1 entries 0..63
+      auto issue_pv_part = [&](int q, int jj, int part) {
         const uint32_t v_base = slot_addr(2 * jj + 1);
         const uint32_t tP = tmem + q * kBN;
         const uint32_t tO = tmem + kColO + q * 128;
 #pragma unroll
-        for (int kb = 0; kb < kBN / 16; ++kb) {
+        for (int k = 0; k < 4; ++k) {
+          const int kb = part == 0 ? 4 + k : k;
           const uint64_t vdesc = tc::smem_desc_sw128(v_base + kb * 2048, kBN * 128, 1024);
           const uint32_t ph = tP + 32 * (kb >> 1) + 8 * (kb & 1);
-          tc::mma_bf16_ts(tO, ph, vdesc, kIdescPV, (jj > 0 || kb > 0) ? 1u : 0u);
+          tc::mma_bf16_ts(tO, ph, vdesc, kIdescPV, (jj > 0 || part > 0 || k > 0) ? 1u : 0u);
           tc::mma_bf16_ts(tO, ph + 16, vdesc, kIdescPV, 1u);
         }
       };
+      // both parts of PV_q(jj), each once the softmax has written that part of P
+      auto issue_pv = [&](int q, int jj) -> bool {
+        for (int part = 0; part < 2; ++part) {
+          if (!wait(p_part + 2 * q + part, uint32_t(jj) & 1u)) return false;
+          tc::fence_after_sync();
+          issue_pv_part(q, jj, part);
+        }
+        return true;
+      };
       bool ok = wait(q_full, 0);
       for (int j = 0; j < ntiles && ok; ++j) {
-        if (!slot_wait(2 * j) || (j > 0 && !slot_wait(2 * j - 1))) {  // K(j), V(j-1)
-          ok = false;
-          break;
-        }
-        fence_proxy_async_smem();
-        tc::fence_after_sync();
         const uint32_t k_base = slot_addr(2 * j);
         for (int q = 0; q < kQTiles; ++q) {
-          if (j > 0) {  // softmax of (q, j-1) done: P_q(j-1) is in TMEM
-            if (!wait(p_full + q, uint32_t(j - 1) & 1u)) {
+          if (q == 0 && j > 0) {  // V(j-1) landed (cp.async writes -> tensor core reads)
+            if (!slot_wait(2 * j - 1)) {
               ok = false;
               break;
             }
+            fence_proxy_async_smem();
+          }
+          if (j > 0 && !issue_pv(q, j - 1)) {  // P_q(j-1) is in TMEM, in two parts
+            ok = false;
+            break;
+          }
+          if (q == 0) {  // K(j) landed
+            if (!slot_wait(2 * j)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_smem();
             tc::fence_after_sync();
-            issue_pv(q, j - 1);
           }
           const uint32_t qb = q_base + q * kQBytes;
 #pragma unroll
@@ -312,14 +334,12 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         tc::commit(slot_empty + (2 * j) % kSlots);                 // K(j) consumed by both QKs
         if (j > 0) tc::commit(slot_empty + (2 * j - 1) % kSlots);  // V(j-1) consumed by both PVs
       }
-      if (ok && ntiles > 0) ok = slot_wait(2 * ntiles - 1);
+      if (ok && ntiles > 0) {
+        ok = slot_wait(2 * ntiles - 1);
+        if (ok) fence_proxy_async_smem();
+      }
       for (int q = 0; q < kQTiles && ok && ntiles > 0; ++q) {
-        if (!wait(p_full + q, uint32_t(ntiles - 1) & 1u)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
-        issue_pv(q, ntiles - 1);
+        if (!issue_pv(q, ntiles - 1)) break;
         tc::commit(o_done + q);
       }
     }
@@ -383,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         m_used = tmax;
         rescale = true;
       }
-      // O_q is quiescent here: PV_q(j-1) completed before s_full(j), PV_q(j) waits for p_full(j)
+      // O_q is quiescent here: PV_q(j-1) completed before s_full(j), PV_q(j) waits for this P
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
         const float a = rescale ? alpha : 1.f;
 #pragma unroll 1
@@ -396,30 +416,60 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           tc::st32(tO + c0, o);
         }
       }
-      const float neg_m = -m_used;
-      float rs = 0.f;
-      // P of the live half (entries 64..127), then of the first half, each over its own columns
-      auto emit_half = [&](int c0) {
+      const uint64_t scale2 = f2_pack(scale, scale), neg_m2 = f2_pack(-m_used, -m_used);
+      uint64_t rs2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};  // packed partial row sums
+      // P of 32 entries written over their own S columns: [0,16) hi pairs, [16,32) lo pairs.
+      // hi = rn_bf16(p), lo = rn_bf16(p - hi), with the scale, the sums and the residual on packed
+      // f32x2 arithmetic.
+      auto emit = [&](const float* xc, int col) {
 #pragma unroll
-        for (int cc = 0; cc < 64; cc += 32) {
-          uint32_t v[32];  // [0,16) hi pairs, [16,32) lo pairs of entries c0 + cc .. + 31
+        for (int sub = 0; sub < 2; ++sub) {  // 16 entries: 8 hi words, 8 lo words
+          uint32_t hi[8], lo[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = fast_exp2(fmaf(x[cc + 2 * i], scale, neg_m));
-            const float p1 = fast_exp2(fmaf(x[cc + 2 * i + 1], scale, neg_m));
-            rs += p0 + p1;
-            split_bf16x2(p0, p1, v[i], v[16 + i]);
+          for (int i = 0; i < 8; ++i) {
+            float t0, t1;
+            f2_unpack(f2_fma(f2_pack(xc[16 * sub + 2 * i], xc[16 * sub + 2 * i + 1]), scale2, neg_m2), t0, t1);
+            const float p0 = fast_exp2(t0), p1 = fast_exp2(t1);
+            const uint64_t pp = f2_pack(p0, p1);
+            rs2[i & 1] = f2_add(rs2[i & 1], pp);
+            hi[i] = pack_bf16x2(p0, p1);
+            const uint64_t hh = f2_pack(__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xffff0000u));
+            float l0, l1;
+            f2_unpack(f2_sub(pp, hh), l0, l1);
+            lo[i] = pack_bf16x2(l0, l1);
           }
-          tc::st32u(tS + c0 + cc, v);
+          tc::st8u(tS + col + 8 * sub, hi);
+          tc::st8u(tS + col + 16 + 8 * sub, lo);
         }
       };
-      emit_half(64);
-      load_half(0);
-      emit_half(0);
-      d_sum = d_sum * alpha + rs;
-      tc::wait_st();  // P (and any rescaled O) in tensor memory before the MMA thread reads them
+      auto mask32 = [&](float* xc, int col) {
+        if (needs_mask) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) xc[c] = col + c < vis ? xc[c] : -INFINITY;
+        }
+      };
+      // x holds entries 64..127; entries 0..63 are read again into each half of x once it is
+      // consumed, overlapping the exponentials and the hand-off.  Each half of P goes to the MMA
+      // thread as soon as it is in tensor memory (with any rescaled O before it).
+      emit(x, 64);
+      tc::ld32(tS, x);
+      emit(x + 32, 96);
+      tc::wait_st();
       tc::fence_before_sync();
-      mbar_arrive(p_full + q);
+      mbar_arrive(p_part + 2 * q);
+      tc::ld32(tS + 32, x + 32);
+      tc::wait_ld();
+      mask32(x, 0);
+      mask32(x + 32, 32);
+      emit(x, 0);
+      emit(x + 32, 32);
+      float r0, r1, r2, r3;
+      f2_unpack(rs2[0], r0, r1);
+      f2_unpack(rs2[1], r2, r3);
+      d_sum = d_sum * alpha + ((r0 + r1) + (r2 + r3));
+      tc::wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(p_part + 2 * q + 1);
     }
     // ---- epilogue: after the last PV of this query tile
     if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, wait(o_done + q, 0));
