@@ -694,27 +694,102 @@ def run_append(args):
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]))
+    clocks.start()
+    time.sleep(0.3)
     a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
         step()
     b_.record()
     torch.cuda.synchronize()
+    clk = clocks.stop()
     ms = a.elapsed_time(b_) / args.steps
     flops = float(sum(16384 * (int(x) * int(p_) + int(x) * (int(x) + 1) / 2) for x, p_ in zip(qlens, pref)))
     tf = flops / (ms / 1e3) / 1e12
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("bf16_tflops", 1590.0))
+
+    # end to end through the reference-facing wrapper: q from pinned host memory, plan + run_return_lse,
+    # outputs and LSE back to pinned host memory, every step
+    from dual_b200.wrapper import BatchPrefillWithPagedKVCacheWrapper
+    wrapper = BatchPrefillWithPagedKVCacheWrapper(torch.empty(1 << 20, dtype=torch.uint8, device=dev), "NHD")
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=torch.bfloat16).pin_memory()
+    lse_host = torch.empty(lse.shape, dtype=torch.float32).pin_memory()
+    qo_t, kv_t = torch.from_numpy(qo), torch.from_numpy(kv)
+    peers = [t for pair in zip(pk, pv) for t in pair]
+    q_dev = torch.empty_like(q)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        wrapper.plan(qo_t, kv_t, full, torch.ones(B, dtype=torch.int32), 32, 8, 128, 1, causal=True,
+                     q_data_type=torch.bfloat16)
+        o_, l_ = wrapper.run_return_lse(q_dev, (k.unsqueeze(1), v.unsqueeze(1)), *peers, full, C, 128 ** -0.5)
+        out_host.copy_(o_, non_blocking=True)
+        lse_host.copy_(l_, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    # traffic: DRAM bytes of one launch from the committed ncu summary of this workload, if any
+    traffic = None
+    tfile = ROOT / "profiles" / "append_traffic.json"
+    if tfile.exists():
+        tj = json.loads(tfile.read_text())
+        if tj.get("workload") == args.workload:
+            traffic = tj.get("dram_bytes_per_launch")
+
+    # CPU baseline: the fp32 oracle on a bounded sample (the last query tokens of the median request
+    # against its whole visible context), scaled by FLOPs
+    from oracle.attention import attend
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    bm = int(np.argsort(lengths)[len(lengths) // 2])
+    qs = min(int(qlens[bm]), 16)
+    Lb = int(lengths[bm])
+    kb_ = torch.randn((Lb, 8, 128)).to(torch.bfloat16)
+    vb_ = torch.randn((Lb, 8, 128)).to(torch.bfloat16)
+    qb_ = torch.randn((qs, 32, 128)).to(torch.bfloat16)
+    pre_s = Lb - qs
+    attend(qb_, kb_, vb_, pre_s, 128 ** -0.5)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 10.0 and reps < 50:
+        attend(qb_, kb_, vb_, pre_s, 128 ** -0.5)
+        reps += 1
+    t_sample = (time.perf_counter() - t0) / reps
+    flops_sample = 16384 * (qs * pre_s + qs * (qs + 1) / 2)
+    cpu_ms = t_sample * flops / flops_sample * 1e3
+
     print(json.dumps({"metric": "causal append attention time per layer", "value": round(ms, 4), "unit": "ms",
-                      "higher_is_better": False, "tflops": round(tf, 1),
+                      "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+                      "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                      "data": "synthetic", "tflops": round(tf, 1),
                       "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
-                                   "frac": round(tf / peak, 4),
-                                   "peak_source": "measured" if peaks else "fallback"},
+                                   "frac": round(tf / peak, 4), "traffic": traffic,
+                                   "kernel": "tiered_append_kernel",
+                                   "peak_source": "measured bf16_tflops" if peaks else "fallback"},
                       "config": {"workload": args.workload, "requests": B, "sum_q": Q, "sum_kv": T,
                                  "remote_tokens": R, "remote_over_local": round(R / (T - R), 4),
                                  "suppliers": [str(o) for o in owners], "work_items": int(work.shape[0]),
-                                 "flops_per_layer": flops},
-                      "status": int(status.item()), "gpu_launches": args.steps}), flush=True)
+                                 "flops_per_layer": flops,
+                                 "l2": "K/V rows gathered from a pool larger than L2; no flush"},
+                      "clocks": clk,
+                      "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": q_host.numel() * 2,
+                              "d2h_bytes_per_step": out_host.numel() * 2 + lse_host.numel() * 4,
+                              "api": "dual_b200.wrapper.BatchPrefillWithPagedKVCacheWrapper.plan/run_return_lse"},
+                      "cpu_baseline": {"value": round(cpu_ms, 1), "unit": "ms", "cores": threads, "kind": "port",
+                                       "sample": f"fp32 oracle: last {qs} query tokens of request {bm} (L={Lb}) "
+                                                 f"against its visible context, scaled by FLOPs"},
+                      "status": int(status.item()) | wrapper.status(), "gpu_launches": args.steps}), flush=True)
 
 # -------------------------------------------------------------- reference arm
 def run_reference(args):
