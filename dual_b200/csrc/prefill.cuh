@@ -31,7 +31,8 @@ struct AppendParams {
   unsigned* status;
 };
 
-// Host-side schedule: one item per (request, kv head, 32-token query tile), costliest first.
+// Host-side schedule: one item {request, kv head, 64-token query pair, kv tiles} per pair, grouped by
+// (request, kv head), groups longest first and pairs longest first within a group.
 // Returns the number of items; writes min(n, max_work) items of 4 int32 into `work` (may be null).
 int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, int batch, int causal, int32_t* work,
                     int64_t max_work);
