@@ -64,6 +64,7 @@ SIGNATURES = {
     "dual_migrate_copy": (C.c_int, [
         VP, VP, C.c_int, C.c_int, VP, VP, C.c_int64, C.c_int, C.c_int64, C.c_int64, C.c_int64, VP, C.c_int,
         C.c_int, VP]),
+    "dual_debug_inject": (C.c_int, [C.c_uint32]),
     "dual_status_clear": (C.c_int, [VP, C.c_int, VP]),
     "dual_status_read": (C.c_int, [VP, U32P, C.c_int, VP]),
     "dual_supplier_alloc": (C.c_int, [C.c_int, C.c_size_t, C.POINTER(VP), C.POINTER(C.c_ubyte)]),

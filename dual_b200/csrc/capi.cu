@@ -1,5 +1,6 @@
 // C ABI entry points (include/dual_b200.h): argument checks, error mapping,
 // kernel launches, IPC / peer access / topology helpers.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -14,6 +15,7 @@
 namespace {
 
 thread_local std::string g_last_error;
+std::atomic<uint32_t> g_inject{0};  // DUAL_INJECT_* bits set by dual_debug_inject (tests only)
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -212,6 +214,7 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.out_stride_head = out_stride_head;
   p.lse = lse;
   p.status = status;
+  p.inject = g_inject.load(std::memory_order_relaxed);
   cudaError_t e = dual::launch_tiered_append(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tiered append launch");
   return DUAL_OK;
@@ -311,6 +314,13 @@ int dual_migrate_copy(const int64_t* local_planes, const int64_t* remote_planes,
   p.status = status;
   cudaError_t e = dual::launch_migrate_copy(p, max_ctas, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "migrate_copy launch");
+  return DUAL_OK;
+}
+
+int dual_debug_inject(uint32_t mask) {
+  g_last_error.clear();
+  if (mask & ~uint32_t(DUAL_INJECT_APPEND_WITHHOLD_K0)) return fail(DUAL_EINVAL, "unknown injection bits 0x%x", mask);
+  g_inject.store(mask, std::memory_order_relaxed);
   return DUAL_OK;
 }
 

@@ -40,6 +40,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "dual_b200.h"
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "tcgen05.cuh"
@@ -251,7 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           cp_async_16_zfill(dst_tile + tc::sw128_offset<kBN>(row, chunk), src + off, valid);
         }
         // arrive on the slot's barrier when this thread's copies have landed; keep issuing ahead
-        cp_async_mbar_arrive_noinc(slot_full + s);
+        // (a test injection withholds the first K tile's arrival: the consumers' waits expire)
+        if (!(u == 0 && (p.inject & DUAL_INJECT_APPEND_WITHHOLD_K0))) cp_async_mbar_arrive_noinc(slot_full + s);
       }
       if (j + 1 < ntiles) {
         resolve(next0, k0, v0);

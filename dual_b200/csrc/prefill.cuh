@@ -29,6 +29,7 @@ struct AppendParams {
   int64_t out_stride_tok, out_stride_head;
   float* lse;                // [sum q, 32] base 2, or nullptr
   unsigned* status;
+  uint32_t inject;           // DUAL_INJECT_* bits (tests only; 0 in production)
 };
 
 // Host-side schedule: one item {request, kv head, 64-token query pair, kv tiles} per pair, grouped by

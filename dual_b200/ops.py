@@ -207,6 +207,15 @@ def migrate_copy(local_planes: torch.Tensor, remote_planes: torch.Tensor, num_pl
         status.data_ptr(), int(max_ctas), dev, _stream(source.device)))
 
 
+def debug_inject(mask: int) -> None:
+    """Test hook: DUAL_INJECT_* bits for the following launches (0 disables; see dual_b200.h)."""
+    _lib.check(_lib.load().dual_debug_inject(int(mask)))
+
+
+INJECT_APPEND_WITHHOLD_K0 = 0x1
+STATUS_WAIT_TIMEOUT = 0x4
+
+
 def status_clear(status: torch.Tensor) -> None:
     lib = _lib.load()
     _lib.check(lib.dual_status_clear(status.data_ptr(), _dev(status), _stream(status.device)))

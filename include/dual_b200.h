@@ -170,6 +170,17 @@ int dual_migrate_copy(const int64_t* local_planes, const int64_t* remote_planes,
                       int reverse, int64_t row_bytes, int64_t local_slots, int64_t remote_slots,
                       uint32_t* status, int max_ctas, int device, void* stream);
 
+/* ------------------------------------------------------ fault injection ---
+ * Test hook with no counterpart in the reference (whose failure handling is fail-fast asserts):
+ * makes a device-side wait run out without faulting the GPU, so tests can check that the
+ * bounded waits turn into DUAL_STATUS_WAIT_TIMEOUT and leave the context usable.  The mask is
+ * process-wide host state read at launch; 0 (the default) disables every injection.
+ *   DUAL_INJECT_APPEND_WITHHOLD_K0: tiered_append loaders never arrive on the barrier of their
+ *   first K tile, so the MMA thread's wait for it expires (~1 s), every role unwinds, and each CTA
+ *   records the timeout in the status word. */
+#define DUAL_INJECT_APPEND_WITHHOLD_K0 0x1u
+int dual_debug_inject(uint32_t mask);
+
 /* --------------------------------------------------------------- status --- */
 int dual_status_clear(uint32_t* status, int device, void* stream);
 /* Synchronous read of a device status word (not capturable). */

@@ -45,6 +45,15 @@ def test_argument_errors_are_codes_not_crashes():
         _lib.check(lib.dual_write_prefill_layout(None, None, 1, 1, None, None, None, None, None, 1, 3, 5, None, -1, None))
 
 
+def test_fault_injection_mask_is_validated():
+    """The test-only injection hook accepts its known bit and 0, refuses anything else (no GPU)."""
+    lib = _lib.load()
+    assert lib.dual_debug_inject(0x80) == 1
+    assert b"injection" in lib.dual_last_error()
+    assert lib.dual_debug_inject(0x1) == 0
+    assert lib.dual_debug_inject(0) == 0
+
+
 def test_workspace_size_formula():
     lib = _lib.load()
     # 256 B header + (G + B) segments x 32 q heads x 132 floats
