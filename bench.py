@@ -27,6 +27,7 @@ import statistics
 import subprocess
 import sys
 import time
+import types
 from pathlib import Path
 
 import numpy as np
@@ -57,7 +58,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["dual", "reference"], default="dual")
-    ap.add_argument("--workload", choices=list(WORKLOADS) + list(TIERED) + ["migration"] + list(APPEND),
+    ap.add_argument("--workload", choices=list(WORKLOADS) + list(TIERED) + ["migration"] + list(APPEND)
+                    + ["fi-" + w for w in list(WORKLOADS) + list(APPEND)],
                     default="config2")
     ap.add_argument("--seed", type=int, default=20261101)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -628,13 +630,13 @@ APPEND = {
 }
 
 
-def run_append(args):
-    """Causal append attention of one layer for the 4-GPU configuration's shapes: per request a
+def append_setup(args, workload):
+    """Inputs of one causal append layer for the 4-GPU configuration's shapes: per request a
     history prefix of P tokens (remote share R/L = 17.97 %, one request in eight ~95 % remote, remote
     only in the history) and q new tokens.  Supplier banks live on GPUs 1..3 when present (peer
     access), else in this GPU's memory.  FLOPs per request = 16384 (q P + q (q + 1) / 2)."""
     from dual_b200 import ops, topology
-    B, qmin, qmax, pmin, pmax, rl, nsup = APPEND[args.workload]
+    B, qmin, qmax, pmin, pmax, rl, nsup = APPEND[workload]
     dev = torch.device("cuda:0")
     ngpu = torch.cuda.device_count()
     owners = [torch.device(f"cuda:{1 + i % (ngpu - 1)}") if ngpu > 1 else dev for i in range(nsup)]
@@ -687,6 +689,20 @@ def run_append(args):
     lse = torch.empty((Q, 32), dtype=torch.float32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     qo_d, kv_d = torch.from_numpy(qo).to(dev), torch.from_numpy(kv).to(dev)
+    flops = float(sum(16384 * (int(x) * int(p_) + int(x) * (int(x) + 1) / 2) for x, p_ in zip(qlens, pref)))
+    return types.SimpleNamespace(B=B, dev=dev, owners=owners, qlens=qlens, pref=pref, lengths=lengths, T=T, R=R, C=C,
+                                 k=k, v=v, pk=pk, pv=pv, full=full, qo=qo, kv=kv, work=work, Q=Q, q=q, out=out, lse=lse,
+                                 status=status, qo_d=qo_d, kv_d=kv_d, flops=flops)
+
+
+def run_append(args):
+    """dual_b200's tiered append kernel on append_setup's inputs (one layer per step)."""
+    from dual_b200 import ops
+    S = append_setup(args, args.workload)
+    B, dev, owners, qlens, pref, lengths, T, R, C = S.B, S.dev, S.owners, S.qlens, S.pref, S.lengths, S.T, S.R, S.C
+    k, v, pk, pv, full, qo, kv, work, Q, q, out, lse, status = (S.k, S.v, S.pk, S.pv, S.full, S.qo, S.kv, S.work, S.Q,
+                                                                 S.q, S.out, S.lse, S.status)
+    qo_d, kv_d = S.qo_d, S.kv_d
 
     def step():
         ops.tiered_append(q, k, v, C, pk, pv, qo_d, kv_d, full, True, 128 ** -0.5, work, out, lse, status)
@@ -705,7 +721,7 @@ def run_append(args):
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = a.elapsed_time(b_) / args.steps
-    flops = float(sum(16384 * (int(x) * int(p_) + int(x) * (int(x) + 1) / 2) for x, p_ in zip(qlens, pref)))
+    flops = S.flops
     tf = flops / (ms / 1e3) / 1e12
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("bf16_tflops", 1590.0))
@@ -791,6 +807,117 @@ def run_append(args):
                                                  f"against its visible context, scaled by FLOPs"},
                       "status": int(status.item()) | wrapper.status(), "gpu_launches": args.steps}), flush=True)
 
+# ------------------------------------------------------- native FlashInfer (the number to beat)
+def run_flashinfer(args):
+    """Native, unpatched FlashInfer FA2 — the kernel the reference runs (BatchDecode with
+    use_tensor_cores=True, peer/backend.py:130; BatchPrefill for append) — on the same inputs as the
+    dual_b200 workload named after the "fi-" prefix, all-local: remote rows are gathered into one
+    local pool first (outside the timed region), as the reference's own oracle does.  Prebuilt by
+    baseline/build_flashinfer.py."""
+    sys.path.insert(0, str(ROOT / "baseline"))
+    import build_flashinfer
+    build_flashinfer.configure()
+    import flashinfer
+    base = args.workload[3:]
+    scale = 128 ** -0.5
+    if base in WORKLOADS:
+        dev = torch.device("cuda:0")
+        args.workload = base
+        w = DecodeWorkload(args, dev)
+        w.ops.pack_read_order(w.tier, w.slot, w.req, w.seq, w.C, 5, 32, w.indices, status=w.status)
+        wrapper = flashinfer.BatchDecodeWithPagedKVCacheWrapper(torch.empty(256 << 20, dtype=torch.uint8, device=dev),
+                                                                "NHD", use_tensor_cores=True, backend="fa2")
+        wrapper.plan(w.indptr, w.indices, torch.ones(w.B, dtype=torch.int32, device=dev), 32, 8, 128, 1,
+                     q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16, sm_scale=scale)
+
+        def step():
+            for i in range(w.layers):
+                wrapper.run(w.q[i], (w.k[i].unsqueeze(1), w.v[i].unsqueeze(1)), out=w.out[i])
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(0)
+        clocks.start()
+        time.sleep(0.3)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        ms = t0.elapsed_time(t1) / args.steps
+        layer_ms = ms / w.layers
+        peak, peak_kind = measured_peaks()
+        gbs = w.bytes_per_layer() / (layer_ms / 1e3) / 1e9
+        print(json.dumps({"impl": "flashinfer-fa2-native", "metric": METRIC, "value": round(w.B / (ms / 1e3), 2),
+                          "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+                          "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": f"{base} inputs, native FlashInfer {flashinfer.__version__} FA2 "
+                                                 f"BatchDecode(use_tensor_cores=True), all-local",
+                                     "batch": w.B, "sum_kv_tokens": w.T, "layers": w.layers},
+                          "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                       "frac": round(gbs / peak, 4), "layer_ms": round(layer_ms, 4),
+                                       "peak_source": f"{peak_kind} hbm_gbs"},
+                          "clocks": clk}), flush=True)
+        return
+    S = append_setup(args, base)
+    dev = S.dev
+    # gather every row of the unified list into one local pool (page 0 unused), outside the timed region
+    full = S.full.long()
+    far = full > S.C
+    n = len(S.pk)
+
+    def gather(local, banks):
+        pool = torch.empty((full.numel() + 1, 8, 128), dtype=torch.bfloat16, device=dev)
+        rows = torch.empty((full.numel(), 8, 128), dtype=torch.bfloat16, device=dev)
+        rows[~far] = local.index_select(0, full[~far])
+        g = full[far] - S.C - 1
+        for d in range(n):
+            m = g % n == d
+            src = banks[d].to(dev).index_select(0, (g[m] // n))
+            idx = torch.nonzero(far).squeeze(1)[m]
+            rows[idx] = src
+        pool[1:] = rows
+        return pool.unsqueeze(1)
+    kp, vp = gather(S.k, S.pk), gather(S.v, S.pv)
+    wrapper = flashinfer.BatchPrefillWithPagedKVCacheWrapper(torch.empty(256 << 20, dtype=torch.uint8, device=dev),
+                                                             "NHD", backend="fa2")
+    wrapper.plan(S.qo_d, S.kv_d, torch.arange(1, full.numel() + 1, dtype=torch.int32, device=dev),
+                 torch.ones(S.B, dtype=torch.int32, device=dev), 32, 8, 128, 1, causal=True, sm_scale=scale,
+                 q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16)
+
+    def step():
+        wrapper.run(S.q, (kp, vp), out=S.out)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    tf = S.flops / (ms / 1e3) / 1e12
+    print(json.dumps({"impl": "flashinfer-fa2-native", "metric": "causal append attention time per layer",
+                      "value": round(ms, 4), "unit": "ms", "n_gpus": 1, "steps": args.steps,
+                      "warmup": max(args.warmup, 3), "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+                      "tflops": round(tf, 1),
+                      "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                                   "frac": round(tf / peak, 4)},
+                      "config": {"workload": f"{base} inputs, native FlashInfer {flashinfer.__version__} FA2 "
+                                             f"BatchPrefill(causal), KV gathered all-local",
+                                 "requests": S.B, "sum_q": S.Q, "sum_kv": S.T, "flops_per_layer": S.flops},
+                      "clocks": clk}), flush=True)
+
+
 # -------------------------------------------------------------- reference arm
 def run_reference(args):
     """The reference's CPU attention math (fp32 torch restatement of check_attention_output,
@@ -847,6 +974,8 @@ def main():
         run_migration(args)
     elif args.workload in APPEND:
         run_append(args)
+    elif args.workload.startswith("fi-"):
+        run_flashinfer(args)
     else:
         run_dual(args)
 
