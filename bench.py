@@ -382,15 +382,16 @@ class TieredWorkload:
     GPU 1's HBM (peer access); per-layer pools of `layers` resident layers (a 36-layer pool of this
     batch does not fit one GPU), the per-step figure is 36 x the per-layer time."""
 
-    def __init__(self, args):
+    def __init__(self, args, compute=0, supplier=1, seed=None):
         from dual_b200 import ops, topology
         from dual_b200.remote_bank import RemoteBank, local_plane_pointers
         self.ops = ops
         B, lmin, lmax, rl, placement, RN, TN, layers, migrate = TIERED[args.workload]
         self.B, self.layers, self.RN, self.TN, self.migrate = B, layers, RN, TN, migrate
-        self.d0, self.d1 = torch.device("cuda:0"), torch.device("cuda:1")
-        topology.enable_peer(0, 1)
-        rng = np.random.default_rng(args.seed)
+        self.d0, self.d1 = torch.device(f"cuda:{compute}"), torch.device(f"cuda:{supplier}")
+        topology.enable_peer(compute, supplier)
+        seed = args.seed if seed is None else seed
+        rng = np.random.default_rng(seed)
         self.lengths = rng.integers(lmin, lmax + 1, B).astype(np.int64)
         self.remote = np.rint(self.lengths * rl / (1.0 + rl)).astype(np.int64)
         self.local = self.lengths - self.remote
@@ -400,13 +401,13 @@ class TieredWorkload:
         C = int(self.local.sum()) + n_bg
         R_cap = self.R + n_bg
         self.C, self.R_cap = C, R_cap
-        g = torch.Generator(device=self.d0).manual_seed(args.seed)
+        g = torch.Generator(device=self.d0).manual_seed(seed)
         self.k = [torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=self.d0) for _ in range(layers)]
         self.v = [torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=self.d0) for _ in range(layers)]
         for t in self.k + self.v:
             t.normal_(generator=g)
         bank_t = torch.empty((layers, 2, R_cap, 8, 128), dtype=torch.bfloat16, device=self.d1)
-        bank_t.normal_(generator=torch.Generator(device=self.d1).manual_seed(args.seed + 1))
+        bank_t.normal_(generator=torch.Generator(device=self.d1).manual_seed(seed + 1))
         self.bank = RemoteBank([bank_t], layers=layers)
         perm = (torch.randperm(C, generator=g, device=self.d0) + 1).to(torch.int32)
         maxL = max(int(self.lengths.max()), n_bg)
@@ -440,7 +441,7 @@ class TieredWorkload:
         self.q = torch.randn((layers, B, 32, 128), generator=g, device=self.d0).to(torch.bfloat16)
         self.out = torch.empty_like(self.q)
         self.lse = torch.empty((layers, B, 32), dtype=torch.float32, device=self.d0)
-        self.num_ctas = ops.default_ctas(0)
+        self.num_ctas = ops.default_ctas(compute)
         self.ws = torch.zeros(ops.decode_workspace_size(B, self.num_ctas), dtype=torch.uint8, device=self.d0)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.d0)
         self.scale = 128 ** -0.5
@@ -507,17 +508,37 @@ class TieredWorkload:
 
 
 def run_tiered(args):
-    if torch.cuda.device_count() < 2:
+    """One (compute, supplier) pair per process.  Under torchrun with W ranks, ranks r < W/2 each
+    decode on GPU r with their supplier bank on GPU r + W/2 (BASELINE config 5 = 4 pairs on 8 GPUs);
+    the other ranks only hold their GPU for the supplier role and join the barriers.  Without
+    torchrun: GPU 0 computes, GPU 1 supplies."""
+    world, rank, local = dist_setup(args)
+    pairs = max(1, world // 2)
+    if world == 1 and torch.cuda.device_count() < 2:
         print(json.dumps({"metric": METRIC, "unavailable": f"{args.workload} needs 2 GPUs"}))
         return
-    w = TieredWorkload(args)
+    is_compute = world == 1 or local < pairs
+    compute, supplier = (0, 1) if world == 1 else (local, local + pairs)
+    if not is_compute:  # supplier rank: its GPU holds a compute rank's bank; take part in the timing collectives
+        dev = torch.device(f"cuda:{local}")
+        torch.cuda.set_device(dev)
+        barrier(world)
+        barrier(world)
+        max_over_ranks(0.0, world, dev)
+        max_over_ranks(0.0, world, dev)
+        import torch.distributed as dist
+        dist.destroy_process_group()
+        return
+    torch.cuda.set_device(compute)
+    w = TieredWorkload(args, compute, supplier, seed=args.seed + 1000 * local)
     stream = torch.cuda.current_stream(w.d0)
     for _ in range(max(args.warmup, 3)):
         w.step()
     torch.cuda.synchronize(w.d0)
-    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]))
+    clocks = ClockSampler(compute)
     clocks.start()
     time.sleep(0.3)
+    barrier(world)
     if w.migrate:
         w.mig_events = []
     all_events = []
@@ -531,20 +552,24 @@ def run_tiered(args):
     t1.record(stream)
     torch.cuda.synchronize(w.d0)
     torch.cuda.synchronize(w.d1)
+    barrier(world)
     clk = clocks.stop()
     layer_ms = [a.elapsed_time(b) for ev in all_events for a, b in ev]
-    t_layer = sum(layer_ms) / len(layer_ms) / 1e3
+    t_layer = max_over_ranks(sum(layer_ms) / len(layer_ms), world, w.d0) / 1e3
+    step_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world, w.d0)
     peak_hbm, peak_kind = measured_peaks()
     t_local = w.local_bytes() / (peak_hbm * 1e9)
     t_remote = w.remote_bytes() / (PEER_GBS * 1e9)
     t_star = max(t_local, t_remote)
-    tok_s = w.B / (36 * t_layer)
+    tok_s = pairs * w.B / (36 * t_layer)
     status = int(w.status.item()) | int(w.ws[:4].view(torch.int32).item())
     result = {
-        "metric": METRIC, "value": round(tok_s, 2), "unit": UNIT, "n_gpus": 2, "steps": args.steps,
+        "metric": METRIC, "value": round(tok_s, 2), "unit": UNIT, "n_gpus": 2 * pairs, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(36 * t_layer * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: 1 compute GPU + 1 KV supplier GPU (peer access), tiered decode",
+        "config": {"workload": f"{args.workload}: {pairs} x (1 compute GPU + 1 KV supplier GPU, peer access), "
+                               f"tiered decode",
+                   "pairs": pairs, "timed_36_layer_equivalent_step_ms": round(36 * step_ms / w.layers, 4),
                    "batch": w.B, "sum_kv_tokens": w.T, "remote_tokens": w.R,
                    "remote_over_local": round(w.R / (w.T - w.R), 4), "read_order_rn_tn": [w.RN, w.TN],
                    "layers_resident": w.layers, "per_step": "36 x per-layer time",
@@ -581,7 +606,11 @@ def run_tiered(args):
         result["migration"]["bit_exact_sampled"] = ok
     if clk:
         result["clocks"] = clk
-    print(json.dumps(result), flush=True)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 # ------------------------------------------------------------ migration copy (1 GPU)
@@ -695,6 +724,34 @@ def append_setup(args, workload):
                                  status=status, qo_d=qo_d, kv_d=kv_d, flops=flops)
 
 
+def append_cpu_baseline(lengths, qlens, flops):
+    """fp32 oracle (the reference's attention math) on a bounded sample: the last query tokens of the
+    median request against its whole visible context, ~10 s, scaled by FLOPs to one layer."""
+    from oracle.attention import attend
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    bm = int(np.argsort(lengths)[len(lengths) // 2])
+    qs = min(int(qlens[bm]), 16)
+    Lb = int(lengths[bm])
+    kb_ = torch.randn((Lb, 8, 128)).to(torch.bfloat16)
+    vb_ = torch.randn((Lb, 8, 128)).to(torch.bfloat16)
+    qb_ = torch.randn((qs, 32, 128)).to(torch.bfloat16)
+    pre_s = Lb - qs
+    attend(qb_, kb_, vb_, pre_s, 128 ** -0.5)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 10.0 and reps < 50:
+        attend(qb_, kb_, vb_, pre_s, 128 ** -0.5)
+        reps += 1
+    t_sample = (time.perf_counter() - t0) / reps
+    flops_sample = 16384 * (qs * pre_s + qs * (qs + 1) / 2)
+    cpu_ms = t_sample * flops / flops_sample * 1e3
+
+    return {"value": round(cpu_ms, 1), "unit": "ms", "cores": threads, "kind": "port",
+            "sample": f"fp32 oracle: last {qs} query tokens of request {bm} (L={Lb}) against its visible context, "
+                      f"scaled by FLOPs"}
+
+
 def run_append(args):
     """dual_b200's tiered append kernel on append_setup's inputs (one layer per step)."""
     from dual_b200 import ops
@@ -728,6 +785,7 @@ def run_append(args):
 
     # end to end through the reference-facing wrapper: q from pinned host memory, plan + run_return_lse,
     # outputs and LSE back to pinned host memory, every step
+    e2e = None
     from dual_b200.wrapper import BatchPrefillWithPagedKVCacheWrapper
     wrapper = BatchPrefillWithPagedKVCacheWrapper(torch.empty(1 << 20, dtype=torch.uint8, device=dev), "NHD")
     q_host = q.cpu().pin_memory()
@@ -745,16 +803,20 @@ def run_append(args):
         out_host.copy_(o_, non_blocking=True)
         lse_host.copy_(l_, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if not args.no_e2e:
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e = {"value": round(e0.elapsed_time(e1) / args.steps, 4), "unit": "ms",
+               "h2d_bytes_per_step": q_host.numel() * 2,
+               "d2h_bytes_per_step": out_host.numel() * 2 + lse_host.numel() * 4,
+               "api": "dual_b200.wrapper.BatchPrefillWithPagedKVCacheWrapper.plan/run_return_lse"}
 
     # traffic: DRAM bytes of one launch from the committed ncu summary of this workload, if any
     traffic = None
@@ -766,25 +828,9 @@ def run_append(args):
 
     # CPU baseline: the fp32 oracle on a bounded sample (the last query tokens of the median request
     # against its whole visible context), scaled by FLOPs
-    from oracle.attention import attend
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    bm = int(np.argsort(lengths)[len(lengths) // 2])
-    qs = min(int(qlens[bm]), 16)
-    Lb = int(lengths[bm])
-    kb_ = torch.randn((Lb, 8, 128)).to(torch.bfloat16)
-    vb_ = torch.randn((Lb, 8, 128)).to(torch.bfloat16)
-    qb_ = torch.randn((qs, 32, 128)).to(torch.bfloat16)
-    pre_s = Lb - qs
-    attend(qb_, kb_, vb_, pre_s, 128 ** -0.5)
-    reps, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < 10.0 and reps < 50:
-        attend(qb_, kb_, vb_, pre_s, 128 ** -0.5)
-        reps += 1
-    t_sample = (time.perf_counter() - t0) / reps
-    flops_sample = 16384 * (qs * pre_s + qs * (qs + 1) / 2)
-    cpu_ms = t_sample * flops / flops_sample * 1e3
-
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = append_cpu_baseline(lengths, qlens, flops)
     print(json.dumps({"metric": "causal append attention time per layer", "value": round(ms, 4), "unit": "ms",
                       "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
                       "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -798,13 +844,7 @@ def run_append(args):
                                  "suppliers": [str(o) for o in owners], "work_items": int(work.shape[0]),
                                  "flops_per_layer": flops,
                                  "l2": "K/V rows gathered from a pool larger than L2; no flush"},
-                      "clocks": clk,
-                      "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": q_host.numel() * 2,
-                              "d2h_bytes_per_step": out_host.numel() * 2 + lse_host.numel() * 4,
-                              "api": "dual_b200.wrapper.BatchPrefillWithPagedKVCacheWrapper.plan/run_return_lse"},
-                      "cpu_baseline": {"value": round(cpu_ms, 1), "unit": "ms", "cores": threads, "kind": "port",
-                                       "sample": f"fp32 oracle: last {qs} query tokens of request {bm} (L={Lb}) "
-                                                 f"against its visible context, scaled by FLOPs"},
+                      "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
                       "status": int(status.item()) | wrapper.status(), "gpu_launches": args.steps}), flush=True)
 
 # ------------------------------------------------------- native FlashInfer (the number to beat)
