@@ -25,6 +25,7 @@ the CPU with the oracle copy).
 """
 from __future__ import annotations
 
+import math
 import time
 from collections import Counter, deque
 from dataclasses import dataclass, field
@@ -93,7 +94,14 @@ class TierManager:
     def __init__(self, tier: torch.Tensor, slot: torch.Tensor, local_capacity: int, remote_capacity: int,
                  numerator: int, denominator: int, copier: Callable, migration_tokens: int = 2048,
                  req_to_token: Optional[torch.Tensor] = None, copy_stream=None, event_factory=None,
-                 main_stream_fn=None):
+                 main_stream_fn=None, remote_cap: Optional[float] = None):
+        """``remote_cap``: optional ceiling on the remote share of each request's live positions.
+        The reference picks victims strictly oldest-first (``peer/policy.py:55``), which pushed its
+        oldest requests to ~95 % remote; capping the share per request is the follow-up its README
+        names (``README.md:128-140``).  None keeps the reference's FIFO."""
+        if remote_cap is not None and not 0.0 < float(remote_cap) <= 1.0:
+            raise ValueError("remote_cap must be in (0, 1]")
+        self.remote_cap = None if remote_cap is None else float(remote_cap)
         self.tier, self.slot = tier, slot
         self.req_to_token = req_to_token
         self.local_capacity, self.remote_capacity = local_capacity, remote_capacity
@@ -181,7 +189,10 @@ class TierManager:
         amount, local, remote, limit = self.amount(needed)
         if amount == 0:
             return None
-        selected = [self.residents.popleft() for _ in range(amount)]
+        selected = self._select_victims(amount, max(0, needed - self.allocator.available_size()))
+        if not selected:
+            return None
+        amount = len(selected)
         if any(self.created[c] >= self.step for c in selected):
             # KV first written by the current forward may still be in flight.
             self.residents.extendleft(reversed(selected))
@@ -220,6 +231,35 @@ class TierManager:
             raise AssertionError("strict remote/local bound violated by the launch")
         self.pending = Pending(selected, sources, source, target, targets, done, record)
         return self.pending
+
+    def _select_victims(self, amount: int, required: int) -> List[Coord]:
+        """Oldest resident positions first; with ``remote_cap``, positions of requests already at
+        their cap are passed over (kept in place) unless the local slots that must be freed
+        (``required``) cannot be found otherwise.  Positions written by the current forward are
+        never eligible under a cap (FIFO raises on them, as the reference asserts)."""
+        if self.remote_cap is None:
+            return [self.residents.popleft() for _ in range(amount)]
+        room: Dict[int, int] = {}
+        chosen: List[Coord] = []
+        passed: Deque[Coord] = deque()
+        while self.residents and len(chosen) < amount:
+            c = self.residents[0]
+            if self.created[c] >= self.step:
+                break  # residents are in creation order: everything after is newer still
+            self.residents.popleft()
+            rid = c[0]
+            if rid not in room:
+                room[rid] = math.floor(self.remote_cap * self.live[rid]) - self.remote_counts[rid]
+            if room[rid] > 0:
+                room[rid] -= 1
+                chosen.append(c)
+            else:
+                passed.append(c)
+        while len(chosen) < required and passed:  # the cap is soft when headroom must be made
+            chosen.append(passed.popleft())
+        chosen.sort(key=lambda k: (self.created[k], k))
+        self.residents.extendleft(reversed(passed))
+        return chosen
 
     def poll(self) -> str:
         """'idle' (nothing in flight), 'pending' (copy running) or 'ready' (commit will not wait)."""
@@ -365,8 +405,10 @@ class TierManager:
         assert bool((f_ >= 0).all()) and bool((f_ < self.remote_capacity).all()), "supplier slot range"
         assert not f_.numel() or self.b * f_.numel() < self.a * n_.numel(), "strict remote/local bound"
         assert +self.remote_counts == Counter(r for r, _ in self.remote_positions), "per-request remote counts"
+        share = max((r["remote"] / r["context"] for r in per_request if r["context"]), default=0.0)
         return dict(local_active_tokens=int(n_.numel()), remote_active_tokens=int(f_.numel()),
-                    logical_tokens=sum(self.live.values()), per_request=per_request, page_tables_exact=True)
+                    logical_tokens=sum(self.live.values()), per_request=per_request, page_tables_exact=True,
+                    max_request_remote_share=share)
 
 
 class _HostEvent:

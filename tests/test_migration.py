@@ -29,13 +29,13 @@ class HostPools:
         return self.local[plane][slot]
 
 
-def _manager(local_cap=200, banks=3, bank_slots=20, a=1797, b=10000, tokens=16, rows=8, ctx=256):
+def _manager(local_cap=200, banks=3, bank_slots=20, a=1797, b=10000, tokens=16, rows=8, ctx=256, cap=None):
     pools = HostPools(4, local_cap, banks, bank_slots)
     tier = torch.full((rows, ctx), -1, dtype=torch.int32)
     slot = torch.zeros_like(tier)
     rtt = torch.zeros_like(tier)
     m = TierManager(tier, slot, local_cap, banks * bank_slots, a, b, pools.copier, migration_tokens=tokens,
-                    req_to_token=rtt)
+                    req_to_token=rtt, remote_cap=cap)
     return m, pools
 
 
@@ -230,3 +230,68 @@ def test_cuda_migration_async_bit_exact_and_decode_unchanged():
     for layer in range(layers):
         after = run_decode(layer)
         torch.testing.assert_close(after.float(), before[layer].float(), atol=2e-3, rtol=1e-2)
+
+
+def _skewed_run(cap):
+    """One old long request and four newer short ones under local pressure (the reference's FIFO
+    pushed its oldest requests to ~95 % remote); migrate until the global budget is used."""
+    m, pools = _manager(local_cap=400, banks=3, bank_slots=40, a=1797, b=10000, tokens=8, rows=6, ctx=400, cap=cap)
+    m.begin_forward()
+    m.append(0, 160)
+    m.begin_forward()
+    for rid in range(1, 5):
+        m.append(rid, 40)
+    before = _snapshot(m, pools)
+    for _ in range(12):
+        m.begin_forward()
+        if m.submit(asynchronous=True) is None:
+            break
+        assert m.poll() == "ready"
+        m.commit()
+        m.audit()
+    after = _snapshot(m, pools)
+    for k, v in before.items():
+        assert np.array_equal(after[k][0], v[0]) and np.array_equal(after[k][1], v[1]), k
+    return m
+
+
+def test_fifo_victims_concentrate_remote_share_on_the_oldest_request():
+    m = _skewed_run(None)
+    info = m.audit()
+    assert info["remote_active_tokens"] > 0
+    shares = {r["request"]: r["remote"] / r["context"] for r in info["per_request"]}
+    assert shares[0] == info["max_request_remote_share"] and all(shares[r] == 0 for r in range(1, 5))
+
+
+def test_remote_cap_spreads_remote_share_and_keeps_every_invariant():
+    fifo = _skewed_run(None).audit()
+    m = _skewed_run(0.15)
+    info = m.audit()
+    assert info["max_request_remote_share"] <= 0.15 + 1e-9
+    assert info["remote_active_tokens"] > 0
+    assert sum(r["remote"] > 0 for r in info["per_request"]) > 1  # more than the oldest request holds remote KV
+    assert info["max_request_remote_share"] < fifo["max_request_remote_share"]
+    local, remote, _ = m.budget()
+    assert 10000 * remote < 1797 * local
+
+
+def test_remote_cap_is_soft_when_local_slots_must_be_freed():
+    m, pools = _manager(local_cap=100, banks=3, bank_slots=40, tokens=16, rows=4, ctx=200, cap=0.05)
+    m.begin_forward()
+    m.append(0, 100)  # local pool full; the cap allows 5 remote positions of request 0
+    before = _snapshot(m, pools)
+    m.begin_forward()
+    m.ensure_headroom(8)  # must free 8 slots: the cap yields to the headroom requirement
+    assert m.allocator.available_size() >= 8
+    info = m.audit()
+    assert info["remote_active_tokens"] >= 8
+    after = _snapshot(m, pools)
+    for k, v in before.items():
+        assert np.array_equal(after[k][0], v[0]) and np.array_equal(after[k][1], v[1]), k
+
+
+def test_remote_cap_rejects_out_of_range_values():
+    with pytest.raises(ValueError):
+        _manager(cap=0.0)
+    with pytest.raises(ValueError):
+        _manager(cap=1.5)
