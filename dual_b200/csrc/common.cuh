@@ -186,6 +186,13 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   return r;
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Hardware base-2 exponential (MUFU.EX2 via the PTX ex2.approx instruction).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

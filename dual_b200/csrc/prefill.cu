@@ -385,14 +385,14 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           for (int c = 0; c < 64; ++c) x[c] = c0 + c < vis ? x[c] : -INFINITY;
         }
       };
-      auto half_max = [&]() {
+      auto half_max = [&]() {  // four independent chains of three-input maxima
         float m4[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-        for (int c = 4; c < 64; c += 4) {
+        for (int c = 4; c < 60; c += 8) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) m4[e] = fmaxf(m4[e], x[c + e]);
+          for (int e = 0; e < 4; ++e) m4[e] = fmax3(m4[e], x[c + e], x[c + 4 + e]);
         }
-        return fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        return fmax3(fmax3(m4[0], m4[1], x[60]), fmax3(m4[2], m4[3], x[61]), fmaxf(x[62], x[63]));
       };
       load_half(0);
       float tmax = half_max();
