@@ -112,8 +112,10 @@ int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_
  * causal != 0 query token i sees entry j iff j < L_b - q_b (history, any order) or
  * j - (L_b - q_b) <= i (the query suffix, in order -- the packer's Full list).
  * dual_append_plan (host): from HOST copies of qo_indptr / kv_indptr, writes the work list
- * (4 int32 per item: request, kv head, 32-token query tile, cost), costliest first; returns the
- * item count in *num_work (call with work=NULL to size it).  The work list is then copied to
+ * (4 int32 per item: request, kv head, 64-token query pair, 128-entry kv tiles), grouped by
+ * (request, kv head) so a group's items run together and share K/V rows in L2, groups longest
+ * first and pairs longest first within a group; returns the item count in *num_work (call with
+ * work=NULL to size it).  The work list is then copied to
  * the device and passed to dual_tiered_append with the DEVICE indptrs.
  * q/out [sum q, 32, 128] bf16; lse [sum q, 32] fp32 base 2 or NULL; status: device word. */
 int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, int batch, int causal,

@@ -171,3 +171,37 @@ def test_prefill_wrapper_reference_convention():
     torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
     torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
     assert w.status() == 0
+
+
+def test_prefill_wrapper_cuda_graph_replay():
+    """plan() builds the work list on the host, so run() is capturable: a graph replayed with new
+    queries in the same buffers matches the oracle."""
+    case = _random_batch(9, B=3)
+    k, v, pk, pv, tier, slot = _dev(case)
+    full, _ = _full_list(tier, slot, case.requests, case.lengths, case.prefixes, case.local_capacity)
+    w = BatchPrefillWithPagedKVCacheWrapper(torch.empty(1 << 20, dtype=torch.uint8, device=DEV), "NHD")
+    qo = torch.tensor(np.concatenate([[0], np.cumsum(case.qlens)]), dtype=torch.int32)
+    kv = torch.tensor(np.concatenate([[0], np.cumsum(case.lengths)]), dtype=torch.int32)
+    w.plan(qo, kv, full, torch.ones(3, dtype=torch.int32), 32, 8, 128, 1, causal=True, q_data_type=torch.bfloat16)
+    peers = [t for pair in zip(pk, pv) for t in pair]
+    q = case.q.to(DEV)
+    out = torch.empty_like(q)
+    lse = torch.empty((q.shape[0], 32), dtype=torch.float32, device=DEV)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        w.run(q, (k.unsqueeze(1), v.unsqueeze(1)), *peers, full, case.local_capacity, 128 ** -0.5, out=out, lse=lse,
+              return_lse=True)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        w.run(q, (k.unsqueeze(1), v.unsqueeze(1)), *peers, full, case.local_capacity, 128 ** -0.5, out=out, lse=lse,
+              return_lse=True)
+    q2 = torch.randn(q.shape, generator=torch.Generator().manual_seed(99)).to(torch.bfloat16)
+    q.copy_(q2)
+    g.replay()
+    torch.cuda.synchronize()
+    ref, ref_lse = OA.tiered_attention(q2, case.k_local, case.v_local, case.peer_k, case.peer_v, case.tier,
+                                       case.slot, case.requests, case.lengths, case.qlens, case.prefixes)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
+    assert w.status() == 0
