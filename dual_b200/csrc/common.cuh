@@ -6,6 +6,7 @@
 // taken from a library; the PTX forms follow the public PTX ISA.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -15,6 +16,21 @@
 #endif
 
 namespace dual {
+
+// Raise a kernel's dynamic shared-memory limit on the current device, once per device.  Function
+// attributes belong to a device's context, so a process that launches on several GPUs must set
+// them on each; `devices` is the caller's per-kernel bitmask of devices already configured.
+template <typename Kernel>
+cudaError_t set_max_dynamic_smem_once(Kernel* kernel, int bytes, std::atomic<uint64_t>& devices) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit != 0 && (devices.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit != 0) devices.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // Error bits written into the device status word (first word of every workspace).
 enum StatusBits : unsigned {

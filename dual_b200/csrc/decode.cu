@@ -347,13 +347,9 @@ int decode_default_grid_g(int device) {
 
 cudaError_t launch_tiered_decode(const TieredDecodeParams& p, cudaStream_t stream) {
   using Cfg = DecodeCfg;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tiered_decode_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (cudaError_t e = set_max_dynamic_smem_once(tiered_decode_kernel<Cfg>, Cfg::SMEM_BYTES, configured))
+    return e;
   tiered_decode_kernel<Cfg><<<p.grid_g, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

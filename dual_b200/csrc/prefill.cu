@@ -559,12 +559,8 @@ int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, int batc
 
 cudaError_t launch_tiered_append(const AppendParams& p, cudaStream_t stream) {
   if (p.num_work <= 0) return cudaSuccess;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tiered_append_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (cudaError_t e = set_max_dynamic_smem_once(tiered_append_kernel, kSmemBytes, configured)) return e;
   tiered_append_kernel<<<p.num_work, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }

@@ -137,3 +137,42 @@ def test_ipc_supplier_process_decode_and_migrate():
         if proc.is_alive():
             proc.kill()
     assert proc.exitcode == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_kernels_launch_on_every_device_of_one_process():
+    """Kernel attributes (the large dynamic shared-memory limit) belong to each device's context:
+    decode and append must launch on a second GPU after the first, in the same process."""
+    case = C.config1(banks=3)
+    for dev_i in (0, 1):
+        d = torch.device(f"cuda:{dev_i}")
+        with torch.cuda.device(d):
+            tier, slot = case.tier.to(d), case.slot.to(d)
+            req = torch.tensor(case.requests, dtype=torch.int32, device=d)
+            seq = torch.tensor(case.lengths, dtype=torch.int32, device=d)
+            idx = torch.empty(sum(case.lengths), dtype=torch.int32, device=d)
+            ops.pack_read_order(tier, slot, req, seq, case.local_capacity, 5, 32, idx)
+            indptr = torch.tensor(np.concatenate([[0], np.cumsum(case.lengths)]), dtype=torch.int32, device=d)
+            k, v = case.k_local.to(d), case.v_local.to(d)
+            pk, pv = [t.to(d) for t in case.peer_k], [t.to(d) for t in case.peer_v]
+            q = case.decode_q().to(d)
+            out = torch.empty((4, 32, 128), dtype=torch.bfloat16, device=d)
+            lse = torch.empty((4, 32), dtype=torch.float32, device=d)
+            ws = torch.zeros(ops.decode_workspace_size(4, ops.default_ctas(dev_i)), dtype=torch.uint8, device=d)
+            ops.tiered_decode(q, k, v, case.local_capacity, pk, pv, indptr, idx, 128 ** -0.5, out, lse, ws)
+            qo = np.arange(5, dtype=np.int32)
+            kv = np.concatenate([[0], np.cumsum(case.lengths)]).astype(np.int32)
+            work = ops.append_plan(qo, kv, True).to(d)
+            out_a = torch.empty_like(q)
+            lse_a = torch.empty((4, 32), dtype=torch.float32, device=d)
+            status = torch.zeros(1, dtype=torch.int32, device=d)
+            ops.tiered_append(q, k, v, case.local_capacity, pk, pv, torch.from_numpy(qo).to(d),
+                              torch.from_numpy(kv).to(d), idx, True, 128 ** -0.5, work, out_a, lse_a, status)
+            torch.cuda.synchronize(d)
+        ref, ref_lse = OA.decode_from_indices(case.decode_q(), case.k_local, case.v_local, case.peer_k, case.peer_v,
+                                              indptr.cpu().tolist(), idx.cpu(), case.local_capacity)
+        torch.testing.assert_close(out.float().cpu(), ref, atol=2e-3, rtol=1e-2)
+        # one query token per request with the whole list visible: the append equals the decode
+        torch.testing.assert_close(out_a.float().cpu(), ref, atol=2e-3, rtol=1e-2)
+        torch.testing.assert_close(lse_a.cpu(), ref_lse, atol=2e-3, rtol=1e-2)
+        assert int(status.item()) == 0 and int(ws[:4].view(torch.int32).item()) == 0
