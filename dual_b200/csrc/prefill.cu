@@ -105,6 +105,10 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 w = p.work[blockIdx.x];
   const int b = w.x, h = w.y, pair = w.z;
+  if (b < 0 || b >= p.batch || h < 0 || h >= kNumKvHeads || pair < 0) {  // a work list from another plan
+    if (tid == 0) atomicOr(p.status, kStatusBadLength);
+    return;
+  }
   const int64_t q0 = p.qo_indptr[b], q_len = int64_t(p.qo_indptr[b + 1]) - q0;
   const int64_t kv0 = p.kv_indptr[b], L = int64_t(p.kv_indptr[b + 1]) - kv0;
   const int64_t t_begin = int64_t(pair) * kPairTok;

@@ -205,3 +205,26 @@ def test_prefill_wrapper_cuda_graph_replay():
     torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
     torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
     assert w.status() == 0
+
+
+def test_stale_work_list_is_a_status_error_not_a_fault():
+    """A work list planned for more requests than the launch has: the out-of-range items are
+    rejected by the kernel's own check (DUAL_STATUS_BAD_LENGTH), the rest still compute."""
+    d = torch.device(DEV)
+    g = torch.Generator().manual_seed(3)
+    lengths, qlens = [300, 200, 150, 100], [40, 30, 20, 10]
+    total = sum(lengths)
+    k = torch.randn((total + 1, 8, 128), generator=g).to(torch.bfloat16).to(d)
+    v = torch.randn((total + 1, 8, 128), generator=g).to(torch.bfloat16).to(d)
+    idx = (torch.randperm(total, generator=g) + 1).int().to(d)
+    qo4 = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    kv4 = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    work = ops.append_plan(qo4, kv4, True).to(d)  # items for 4 requests
+    qo2, kv2 = torch.from_numpy(qo4[:3].copy()).to(d), torch.from_numpy(kv4[:3].copy()).to(d)  # launch has 2
+    q = torch.randn((int(qo4[2]), 32, 128), generator=g).to(torch.bfloat16).to(d)
+    out = torch.zeros_like(q)
+    lse = torch.zeros((q.shape[0], 32), dtype=torch.float32, device=d)
+    status = torch.zeros(1, dtype=torch.int32, device=d)
+    ops.tiered_append(q, k, v, total, [], [], qo2, kv2, idx, True, 128 ** -0.5, work, out, lse, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 0x10  # DUAL_STATUS_BAD_LENGTH
