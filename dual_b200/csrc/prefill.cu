@@ -306,25 +306,18 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       bool ok = wait(q_full, 0);
       for (int j = 0; j < ntiles && ok; ++j) {
         const uint32_t k_base = slot_addr(2 * j);
+        // K(j) landed, and with it V(j-1): each loader thread issues V(j-1) before K(j) and arrives
+        // on K(j)'s barrier only once all of its earlier copies have landed (one poll, not two)
+        if (!slot_wait(2 * j)) {
+          ok = false;
+          break;
+        }
+        fence_proxy_async_smem();  // cp.async writes -> tensor core reads
+        tc::fence_after_sync();
         for (int q = 0; q < kQTiles; ++q) {
-          if (q == 0 && j > 0) {  // V(j-1) landed (cp.async writes -> tensor core reads)
-            if (!slot_wait(2 * j - 1)) {
-              ok = false;
-              break;
-            }
-            fence_proxy_async_smem();
-          }
           if (j > 0 && !issue_pv(q, j - 1)) {  // P_q(j-1) is in TMEM, in two parts
             ok = false;
             break;
-          }
-          if (q == 0) {  // K(j) landed
-            if (!slot_wait(2 * j)) {
-              ok = false;
-              break;
-            }
-            fence_proxy_async_smem();
-            tc::fence_after_sync();
           }
           const uint32_t qb = q_base + q * kQBytes;
 #pragma unroll
