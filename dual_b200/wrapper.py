@@ -138,8 +138,8 @@ class BatchPrefillWithPagedKVCacheWrapper:
     """Paged append / prefill attention (page_size 1, NHD), FlashInfer's plan/run convention.
 
     ``plan`` takes the (host or device) ``qo_indptr`` / ``paged_kv_indptr`` like FlashInfer's planner,
-    builds the costliest-first work list on the host and uploads it; ``run`` launches the tcgen05
-    append kernel.  The reference passes the same tiered tail as for decode
+    builds the work list on the host (one item per request x kv head x 64 query tokens, grouped by
+    request and kv head, longest first) and uploads it; ``run`` launches the tcgen05 append kernel.  The reference passes the same tiered tail as for decode
     (peer/prefill_backend.py:25-37): ``run(q, paged_kv, *peers, indices, local_capacity, sm_scale)``,
     where ``indices`` is the packer's Full list (causal, non-ragged) or History list (ragged cascade).
     """
