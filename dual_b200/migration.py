@@ -61,6 +61,30 @@ class LocalAllocator:
         self._free.extend(int(s) for s in slots)
 
 
+class SGLangAllocatorAdapter:
+    """Drives TierManager with SGLang's own KV slot allocator (``token_to_kv_pool_allocator``:
+    ``alloc(n)`` returns an index tensor or None, ``free(indices)`` takes one, ``available_size()``),
+    so migrated-out local slots go back to the allocator SGLang's scheduler uses for new tokens
+    (the reference frees them there too, V/nvlink_prefill_timing/backend.py:34,42)."""
+
+    def __init__(self, allocator, device=None):
+        self.inner = allocator
+        self.device = device
+
+    def available_size(self) -> int:
+        return int(self.inner.available_size())
+
+    def alloc(self, n: int) -> Optional[List[int]]:
+        out = self.inner.alloc(n)
+        if out is None:
+            return None
+        return [int(x) for x in (out.tolist() if hasattr(out, "tolist") else out)]
+
+    def free(self, slots: Sequence[int]) -> None:
+        if len(slots):
+            self.inner.free(torch.tensor(list(slots), dtype=torch.int64, device=self.device))
+
+
 @dataclass
 class Pending:
     coords: List[Coord]
@@ -94,11 +118,14 @@ class TierManager:
     def __init__(self, tier: torch.Tensor, slot: torch.Tensor, local_capacity: int, remote_capacity: int,
                  numerator: int, denominator: int, copier: Callable, migration_tokens: int = 2048,
                  req_to_token: Optional[torch.Tensor] = None, copy_stream=None, event_factory=None,
-                 main_stream_fn=None, remote_cap: Optional[float] = None):
+                 main_stream_fn=None, remote_cap: Optional[float] = None, allocator=None):
         """``remote_cap``: optional ceiling on the remote share of each request's live positions.
         The reference picks victims strictly oldest-first (``peer/policy.py:55``), which pushed its
         oldest requests to ~95 % remote; capping the share per request is the follow-up its README
-        names (``README.md:128-140``).  None keeps the reference's FIFO."""
+        names (``README.md:128-140``).  None keeps the reference's FIFO.
+        ``allocator``: the local slot allocator to draw from and free into (``LocalAllocator``
+        interface, e.g. ``SGLangAllocatorAdapter`` around SGLang's); None = a private free list over
+        slots 1..local_capacity."""
         if remote_cap is not None and not 0.0 < float(remote_cap) <= 1.0:
             raise ValueError("remote_cap must be in (0, 1]")
         self.remote_cap = None if remote_cap is None else float(remote_cap)
@@ -108,7 +135,8 @@ class TierManager:
         self.a, self.b = numerator, denominator
         self.copy = copier
         self.migration_tokens = migration_tokens
-        self.allocator = LocalAllocator(local_capacity)
+        self._external_allocator = allocator
+        self.allocator = allocator if allocator is not None else LocalAllocator(local_capacity)
         self.device = tier.device
         cuda = self.device.type == "cuda"
         self.copy_stream = copy_stream if copy_stream is not None else (torch.cuda.Stream(self.device) if cuda else None)
@@ -121,7 +149,8 @@ class TierManager:
     def reset(self) -> None:
         self.tier.fill_(-1)
         self.slot.zero_()
-        self.allocator = LocalAllocator(self.local_capacity)
+        # an external allocator (SGLang's) keeps its own state; only the private free list restarts
+        self.allocator = self._external_allocator or LocalAllocator(self.local_capacity)
         self.live: Dict[int, int] = {}
         self.residents: Deque[Coord] = deque()
         self.created: Dict[Coord, int] = {}

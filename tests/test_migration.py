@@ -295,3 +295,52 @@ def test_remote_cap_rejects_out_of_range_values():
         _manager(cap=0.0)
     with pytest.raises(ValueError):
         _manager(cap=1.5)
+
+
+class FakeSGLangAllocator:
+    """SGLang's token_to_kv_pool_allocator interface: a free-page tensor, alloc slices, free concatenates."""
+
+    def __init__(self, size):
+        self.free_pages = torch.arange(1, size + 1, dtype=torch.int64)
+
+    def available_size(self):
+        return len(self.free_pages)
+
+    def alloc(self, need_size):
+        if need_size > len(self.free_pages):
+            return None
+        out, self.free_pages = self.free_pages[:need_size], self.free_pages[need_size:]
+        return out
+
+    def free(self, free_index):
+        self.free_pages = torch.cat((self.free_pages, free_index.to(torch.int64)))
+
+
+def test_tier_manager_drives_sglangs_allocator():
+    from dual_b200.migration import SGLangAllocatorAdapter
+    pools = HostPools(4, 200, 3, 20)
+    tier = torch.full((8, 256), -1, dtype=torch.int32)
+    slot = torch.zeros_like(tier)
+    rtt = torch.zeros_like(tier)
+    fake = FakeSGLangAllocator(200)
+    m = TierManager(tier, slot, 200, 60, 1797, 10000, pools.copier, migration_tokens=16, req_to_token=rtt,
+                    allocator=SGLangAllocatorAdapter(fake))
+    for rid in range(4):
+        m.begin_forward()
+        m.append(rid, 40)
+    assert fake.available_size() == 40
+    before = _snapshot(m, pools)
+    m.begin_forward()
+    m.submit()
+    m.commit()
+    assert fake.available_size() == 56  # migrated-out local slots went back to SGLang's allocator
+    info = m.audit()
+    assert info["remote_active_tokens"] == 16
+    after = _snapshot(m, pools)
+    for k, v in before.items():
+        assert np.array_equal(after[k][0], v[0]) and np.array_equal(after[k][1], v[1]), k
+    m.release([0])
+    assert fake.available_size() == 56 + 24  # request 0's remaining local slots
+    m.audit()
+    m.reset()
+    assert m.allocator.inner is fake  # SGLang's allocator is not replaced
