@@ -10,7 +10,11 @@ packer (unified read order for the batch) + 36 layers of tiered decode
 (decode kernel + merge).  Per-layer KV (4.5 GB) is far larger than L2, so no
 flush is needed between iterations.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dual|reference] [--workload config2|small]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dual|reference] [--workload W]
+
+Workloads: config2 (default), small; config3, config5, tiered-small (a compute GPU + a supplier GPU;
+under torchrun N/2 such pairs); config4, append-small, append-mid (causal append); migration;
+fi-<workload> times native FlashInfer FA2 on the same inputs (the number to beat).
 
 Under torchrun (N > 1) every rank serves its own independent batch (decode
 shards by request; no collective on the data path): scaling "weak".
@@ -48,6 +52,8 @@ WORKLOADS = {
 TIERED = {
     "config3": (128, 2048, 32768, 0.0599, "tail", 8, 128, 6, False),
     "config5": (128, 4096, 32768, 0.1797, "prefix", 5, 32, 6, True),
+    # profiling case: config-5 ratios and read order, 16 requests, 2 resident layers (~3 GB on the device)
+    "tiered-small": (16, 4096, 32768, 0.1797, "prefix", 5, 32, 2, False),
 }
 PEER_GBS = 770.0  # measured peer copy per direction on this pool (NVLink 5, NVSwitch)
 
