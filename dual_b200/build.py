@@ -17,6 +17,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIBDIR = PKG / "lib"
 LIBNAME = "libdual_b200.so"
+SUPPLIER = "dual_supplier"  # native KV-supplier process (supplier_service.cpp)
 SOURCES = ["capi.cu", "decode.cu", "decode_noalloc.cu", "pack.cu", "migrate.cu", "prefill.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -36,14 +37,20 @@ def _stale(target: Path) -> bool:
     if not target.exists():
         return True
     mtime = target.stat().st_mtime
-    deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + [ROOT / "include" / "dual_b200.h"]
+    deps = (list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.cpp"))
+            + [ROOT / "include" / "dual_b200.h"])
     return any(d.stat().st_mtime > mtime for d in deps if d.exists())
 
 
+def supplier_path() -> Path:
+    return LIBDIR / SUPPLIER
+
+
 def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    """Compile every CUDA source into the shared library (skipped when up to date)."""
+    """Compile every CUDA source into the shared library and the native supplier executable
+    (skipped when up to date)."""
     target = library_path()
-    if not force and not _stale(target):
+    if not force and not _stale(target) and not _stale(supplier_path()):
         return target
     LIBDIR.mkdir(parents=True, exist_ok=True)
     objdir = ROOT / "_build" / "obj"
@@ -70,6 +77,13 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
     tmp.replace(target)
+    exe_tmp = LIBDIR / (SUPPLIER + ".tmp")
+    cmd = [nvcc(), *ARCH, "-O2", "-std=c++17", "-I", str(ROOT / "include"), str(CSRC / "supplier_service.cpp"),
+           "-o", str(exe_tmp), "-cudart", "static"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"dual_supplier build failed:\n{res.stdout}\n{res.stderr}")
+    exe_tmp.replace(supplier_path())
     return target
 
 

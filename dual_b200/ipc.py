@@ -24,7 +24,12 @@ product path; tests run the same protocol on CPU with file-backed shared memory.
 from __future__ import annotations
 
 import ctypes as C
+import json
+import socket
+import subprocess
+import time
 import traceback
+from pathlib import Path
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -120,6 +125,79 @@ class DistChannel:
         buf = [None]
         dist.recv_object_list(buf, src=self.peer, group=self.group)  # bounded by the group's timeout
         return buf[0]
+
+
+class SocketChannel:
+    """One JSON object per line over a Unix-domain socket: the channel of the native supplier
+    process (``dual_b200/lib/dual_supplier``, supplier_service.cpp).  The 64-byte handle travels
+    as hex.  Connecting retries until the supplier listens (bounded), and fails early if the
+    supplier process has already exited."""
+
+    def __init__(self, path, connect_timeout: float = 60.0, process=None):
+        deadline = time.monotonic() + connect_timeout
+        while True:
+            s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+            try:
+                s.connect(str(path))
+                break
+            except (FileNotFoundError, ConnectionRefusedError):
+                s.close()
+                if process is not None and process.poll() is not None:
+                    err = process.stderr.read().decode(errors="replace") if process.stderr else ""
+                    raise RuntimeError(f"supplier process exited ({process.returncode}) before listening: {err}")
+                if time.monotonic() > deadline:
+                    raise TimeoutError(f"no supplier listening on {path} within {connect_timeout:.1f} s")
+                time.sleep(0.02)
+        self.sock, self.buf = s, b""
+
+    def send(self, obj) -> None:
+        self.sock.sendall((json.dumps(obj) + "\n").encode())
+
+    def recv(self, timeout: Optional[float]):
+        deadline = None if timeout is None else time.monotonic() + timeout
+        while b"\n" not in self.buf:
+            left = None if deadline is None else deadline - time.monotonic()
+            if left is not None and left <= 0:
+                raise TimeoutError(f"no message from the supplier within {timeout:.1f} s")
+            self.sock.settimeout(left)
+            try:
+                data = self.sock.recv(65536)
+            except socket.timeout:
+                raise TimeoutError(f"no message from the supplier within {timeout:.1f} s") from None
+            if not data:
+                raise RuntimeError("the supplier closed the connection")
+            self.buf += data
+        line, self.buf = self.buf.split(b"\n", 1)
+        msg = json.loads(line)
+        if isinstance(msg.get("handle"), str):
+            msg["handle"] = bytes.fromhex(msg["handle"])
+        return msg
+
+    def close(self) -> None:
+        self.sock.close()
+
+
+def spawn_native_supplier(socket_path, role: int, device: int, layers: int, slots: int, backend: str = "cuda",
+                          directory=None, timeout: float = 120.0, close_timeout: Optional[float] = None):
+    """Start the native supplier process for one bank and connect to it: (process, SocketChannel).
+    The caller waits for the process after ``close_suppliers`` (it exits 0 once it has freed the
+    bank) or kills that exact process on failure."""
+    exe = Path(__file__).resolve().parent / "lib" / "dual_supplier"
+    if not exe.exists():
+        raise RuntimeError(f"{exe} is not built (python -m dual_b200.build)")
+    cmd = [str(exe), "--socket", str(socket_path), "--role", str(role), "--device", str(device),
+           "--layers", str(layers), "--slots", str(slots), "--backend", backend, "--timeout", str(timeout)]
+    if directory is not None:
+        cmd += ["--dir", str(directory)]
+    if close_timeout is not None:
+        cmd += ["--close-timeout", str(close_timeout)]
+    proc = subprocess.Popen(cmd, stdout=subprocess.DEVNULL, stderr=subprocess.PIPE)
+    try:
+        return proc, SocketChannel(socket_path, connect_timeout=timeout, process=proc)
+    except BaseException:
+        proc.kill()
+        proc.wait()
+        raise
 
 
 def _expect(msg, kind: str):

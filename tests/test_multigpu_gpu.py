@@ -176,3 +176,30 @@ def test_kernels_launch_on_every_device_of_one_process():
         torch.testing.assert_close(out_a.float().cpu(), ref, atol=2e-3, rtol=1e-2)
         torch.testing.assert_close(lse_a.cpu(), ref_lse, atol=2e-3, rtol=1e-2)
         assert int(status.item()) == 0 and int(ws[:4].view(torch.int32).item()) == 0
+
+
+def test_native_supplier_process_decode(tmp_path):
+    """The native supplier executable owns the bank on GPU 1 (cudaMalloc + cudaIpcGetMemHandle);
+    the compute side imports it through the same handshake, decodes against the oracle, and the
+    supplier frees the bank and exits 0 after close."""
+    layers, slots = 1, 4096
+    proc, ch = ipc.spawn_native_supplier(tmp_path / "sup.sock", 0, 1, layers, slots, backend="cuda", timeout=120.0)
+    try:
+        bank, ptrs = ipc.open_suppliers([ch], 0, layers, slots, timeout=120)
+        case = C.config1(banks=1)
+        d0 = torch.device("cuda:0")
+        n_remote = case.peer_k[0].shape[0]
+        bank.banks[0][0, 0, :n_remote].copy_(case.peer_k[0].to(d0))
+        bank.banks[0][0, 1, :n_remote].copy_(case.peer_v[0].to(d0))
+        out, lse, indptr, idx, ws = _decode(case.decode_q().to(d0), case.k_local.to(d0), case.v_local.to(d0),
+                                            [bank.banks[0][0, 0]], [bank.banks[0][0, 1]], case.lengths,
+                                            case.tier.to(d0), case.slot.to(d0), case.requests, case.local_capacity)
+        ref, _ = OA.decode_from_indices(case.decode_q(), case.k_local, case.v_local, case.peer_k, case.peer_v,
+                                        indptr.cpu().tolist(), idx.cpu(), case.local_capacity)
+        torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+        ipc.close_suppliers([ch], 0, ptrs, timeout=120)
+        assert proc.wait(timeout=120) == 0
+    finally:
+        if proc.poll() is None:
+            proc.kill()
+            proc.wait()
