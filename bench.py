@@ -70,6 +70,10 @@ def parse():
     ap.add_argument("--seed", type=int, default=20261101)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--stage", choices=["range", "rows"], default=None,
+                    help="append workloads: stage each layer's supplier rows into local memory first "
+                         "(LayerStager: 'range' = copy engines, one stream per bank, overlapped with the "
+                         "previous layer's append; 'rows' = the row kernel before each append)")
     return ap.parse_args()
 
 
@@ -766,20 +770,48 @@ def run_append(args):
     k, v, pk, pv, full, qo, kv, work, Q, q, out, lse, status = (S.k, S.v, S.pk, S.pv, S.full, S.qo, S.kv, S.work, S.Q,
                                                                  S.q, S.out, S.lse, S.status)
     qo_d, kv_d = S.qo_d, S.kv_d
+    warm = max(args.warmup, 3)
 
-    def step():
-        ops.tiered_append(q, k, v, C, pk, pv, qo_d, kv_d, full, True, 128 ** -0.5, work, out, lse, status)
+    # Supplier rows either read in place (peer loads from the banks) or, with --stage, copied once per
+    # layer into local buffers by the LayerStager on a side stream while the previous layer's append
+    # runs.  Every step is one layer of a forward; the stager's start() (layer 0's copy, not overlapped)
+    # is inside the timed region.
+    stager = None
+    if args.stage:
+        from dual_b200.staging import LayerStager
+        stager = LayerStager(lambda i: (pk, pv), max(warm, args.steps), dev, depth=2, mode=args.stage)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
+    def begin():
+        if stager is not None:
+            stager.start(full, C)
+
+    def banks(i):
+        if stager is None:
+            return pk, pv
+        t = stager.tail(i)
+        return t[0::2], t[1::2]
+
+    def done(i):
+        if stager is not None:
+            stager.next(i)
+
+    def step(i):
+        bk, bv = banks(i)
+        ops.tiered_append(q, k, v, C, bk, bv, qo_d, kv_d, full, True, 128 ** -0.5, work, out, lse, status)
+        done(i)
+
+    begin()
+    for i in range(warm):
+        step(i)
     torch.cuda.synchronize()
     clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]))
     clocks.start()
     time.sleep(0.3)
     a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(args.steps):
-        step()
+    begin()
+    for i in range(args.steps):
+        step(i)
     b_.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -801,22 +833,26 @@ def run_append(args):
     peers = [t for pair in zip(pk, pv) for t in pair]
     q_dev = torch.empty_like(q)
 
-    def e2e_step():
+    def e2e_step(i):
         q_dev.copy_(q_host, non_blocking=True)
         wrapper.plan(qo_t, kv_t, full, torch.ones(B, dtype=torch.int32), 32, 8, 128, 1, causal=True,
                      q_data_type=torch.bfloat16)
-        o_, l_ = wrapper.run_return_lse(q_dev, (k.unsqueeze(1), v.unsqueeze(1)), *peers, full, C, 128 ** -0.5)
+        tail = peers if stager is None else stager.tail(i)
+        o_, l_ = wrapper.run_return_lse(q_dev, (k.unsqueeze(1), v.unsqueeze(1)), *tail, full, C, 128 ** -0.5)
+        done(i)
         out_host.copy_(o_, non_blocking=True)
         lse_host.copy_(l_, non_blocking=True)
 
     if not args.no_e2e:
-        for _ in range(2):
-            e2e_step()
+        begin()
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
-            e2e_step()
+        begin()
+        for i in range(args.steps):
+            e2e_step(i)
         e1.record()
         torch.cuda.synchronize()
         e2e = {"value": round(e0.elapsed_time(e1) / args.steps, 4), "unit": "ms",
@@ -849,9 +885,16 @@ def run_append(args):
                                  "remote_tokens": R, "remote_over_local": round(R / (T - R), 4),
                                  "suppliers": [str(o) for o in owners], "work_items": int(work.shape[0]),
                                  "flops_per_layer": flops,
+                                 "supplier_rows": ({"range": "staged: LayerStager 'range', whole banks copied by "
+                                                             "the copy engines per layer, one stream per bank, "
+                                                             "overlapped with the previous layer's append",
+                                                    "rows": "staged: LayerStager 'rows', the rows the index list "
+                                                            "names copied by the row kernel before each append"}
+                                                   [args.stage] if stager is not None else "read in place"),
                                  "l2": "K/V rows gathered from a pool larger than L2; no flush"},
                       "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
-                      "status": int(status.item()) | wrapper.status(), "gpu_launches": args.steps}), flush=True)
+                      "status": int(status.item()) | wrapper.status() | (stager.status() if stager else 0),
+                      "gpu_launches": args.steps * (2 if args.stage == "rows" else 1)}), flush=True)
 
 # ------------------------------------------------------- native FlashInfer (the number to beat)
 def run_flashinfer(args):

@@ -64,6 +64,12 @@ SIGNATURES = {
     "dual_migrate_copy": (C.c_int, [
         VP, VP, C.c_int, C.c_int, VP, VP, C.c_int64, C.c_int, C.c_int64, C.c_int64, C.c_int64, VP, C.c_int,
         C.c_int, VP]),
+    "dual_stage_remote_rows": (C.c_int, [
+        VP, VP, VP, VP, C.c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int64,  # banks, stages, n, strides, slots, row
+        VP, C.c_int64, C.c_int64, VP, C.c_int, C.c_int, VP]),  # indices, n, C, status, max_ctas, device, stream
+    "dual_stage_bank_range": (C.c_int, [
+        VP, VP, VP, VP, C.c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int64,  # banks, stages, n, strides, slots, row
+        VP, VP, VP, C.c_int]),  # row_begin, row_end, streams, device
     "dual_debug_inject": (C.c_int, [C.c_uint32]),
     "dual_status_clear": (C.c_int, [VP, C.c_int, VP]),
     "dual_status_read": (C.c_int, [VP, U32P, C.c_int, VP]),

@@ -11,6 +11,7 @@
 #include "migrate.cuh"
 #include "pack.cuh"
 #include "prefill.cuh"
+#include "stage.cuh"
 
 namespace {
 
@@ -217,6 +218,93 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.inject = g_inject.load(std::memory_order_relaxed);
   cudaError_t e = dual::launch_tiered_append(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tiered append launch");
+  return DUAL_OK;
+}
+
+int dual_stage_remote_rows(const void* const* peer_k, const void* const* peer_v, void* const* stage_k,
+                           void* const* stage_v, int num_banks, int64_t peer_stride_bytes,
+                           int64_t stage_stride_bytes, int64_t bank_slots, int64_t row_bytes,
+                           const int32_t* unified_indices, int64_t num_indices, int64_t local_capacity,
+                           uint32_t* status, int max_ctas, int device, void* stream) {
+  g_last_error.clear();
+  if (num_indices < 0) return fail(DUAL_EINVAL, "num_indices must be >= 0");
+  if (num_indices == 0) return DUAL_OK;
+  if (!unified_indices || !status) return fail(DUAL_EINVAL, "null pointer argument");
+  if (num_banks <= 0 || num_banks > dual::kMaxPeers)
+    return fail(DUAL_EINVAL, "num_banks must be in [1, %d] (got %d)", dual::kMaxPeers, num_banks);
+  if (!peer_k || !peer_v || !stage_k || !stage_v) return fail(DUAL_EINVAL, "bank / stage pointer arrays are null");
+  if (row_bytes <= 0 || (row_bytes & 15)) return fail(DUAL_EINVAL, "row_bytes must be a positive multiple of 16");
+  if ((peer_stride_bytes & 15) || (stage_stride_bytes & 15) || peer_stride_bytes < row_bytes ||
+      stage_stride_bytes < row_bytes)
+    return fail(DUAL_EINVAL, "strides must be multiples of 16 bytes and at least row_bytes");
+  if (bank_slots <= 0) return fail(DUAL_EINVAL, "bank_slots must be positive");
+  if (local_capacity < 0 || local_capacity > 0xfffffffeLL) return fail(DUAL_EINVAL, "local_capacity out of range");
+  for (int i = 0; i < num_banks; ++i)
+    if (!peer_k[i] || !peer_v[i] || !stage_k[i] || !stage_v[i] || !aligned16(peer_k[i]) || !aligned16(peer_v[i]) ||
+        !aligned16(stage_k[i]) || !aligned16(stage_v[i]))
+      return fail(DUAL_EINVAL, "bank %d: bank or stage pointer null or not 16-byte aligned", i);
+  if (int rc = set_device(device)) return rc;
+  dual::StageParams p{};
+  for (int i = 0; i < dual::kMaxPeers; ++i) {
+    p.peer_k[i] = i < num_banks ? static_cast<const char*>(peer_k[i]) : nullptr;
+    p.peer_v[i] = i < num_banks ? static_cast<const char*>(peer_v[i]) : nullptr;
+    p.stage_k[i] = i < num_banks ? static_cast<char*>(stage_k[i]) : nullptr;
+    p.stage_v[i] = i < num_banks ? static_cast<char*>(stage_v[i]) : nullptr;
+  }
+  p.banks = num_banks;
+  p.peer_stride = peer_stride_bytes;
+  p.stage_stride = stage_stride_bytes;
+  p.bank_slots = bank_slots;
+  p.row_bytes = row_bytes;
+  p.indices = unified_indices;
+  p.n = num_indices;
+  p.local_capacity = local_capacity;
+  p.status = status;
+  cudaError_t e = dual::launch_stage_rows(p, max_ctas, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "stage_remote_rows launch");
+  return DUAL_OK;
+}
+
+int dual_stage_bank_range(const void* const* peer_k, const void* const* peer_v, void* const* stage_k,
+                          void* const* stage_v, int num_banks, int64_t peer_stride_bytes,
+                          int64_t stage_stride_bytes, int64_t bank_slots, int64_t row_bytes,
+                          const int64_t* row_begin, const int64_t* row_end, void* const* streams, int device) {
+  g_last_error.clear();
+  if (num_banks <= 0 || num_banks > dual::kMaxPeers)
+    return fail(DUAL_EINVAL, "num_banks must be in [1, %d] (got %d)", dual::kMaxPeers, num_banks);
+  if (!peer_k || !peer_v || !stage_k || !stage_v || !row_begin || !row_end || !streams)
+    return fail(DUAL_EINVAL, "null pointer argument");
+  if (row_bytes <= 0 || (row_bytes & 15)) return fail(DUAL_EINVAL, "row_bytes must be a positive multiple of 16");
+  if ((peer_stride_bytes & 15) || (stage_stride_bytes & 15) || peer_stride_bytes < row_bytes ||
+      stage_stride_bytes < row_bytes)
+    return fail(DUAL_EINVAL, "strides must be multiples of 16 bytes and at least row_bytes");
+  if (bank_slots <= 0) return fail(DUAL_EINVAL, "bank_slots must be positive");
+  for (int i = 0; i < num_banks; ++i) {
+    if (!peer_k[i] || !peer_v[i] || !stage_k[i] || !stage_v[i])
+      return fail(DUAL_EINVAL, "bank %d: bank or stage pointer is null", i);
+    if (row_begin[i] < 0 || row_end[i] > bank_slots || row_begin[i] > row_end[i])
+      return fail(DUAL_EINVAL, "bank %d: row range [%lld, %lld) outside [0, %lld]", i, (long long)row_begin[i],
+                  (long long)row_end[i], (long long)bank_slots);
+  }
+  if (int rc = set_device(device)) return rc;
+  for (int i = 0; i < num_banks; ++i) {
+    const int64_t rows = row_end[i] - row_begin[i];
+    if (rows == 0) continue;
+    cudaStream_t st = static_cast<cudaStream_t>(streams[i]);
+    const void* src[2] = {peer_k[i], peer_v[i]};
+    void* dst[2] = {stage_k[i], stage_v[i]};
+    for (int plane = 0; plane < 2; ++plane) {
+      const char* s = static_cast<const char*>(src[plane]) + row_begin[i] * peer_stride_bytes;
+      char* d = static_cast<char*>(dst[plane]) + row_begin[i] * stage_stride_bytes;
+      cudaError_t e;
+      if (peer_stride_bytes == row_bytes && stage_stride_bytes == row_bytes)
+        e = cudaMemcpyAsync(d, s, size_t(rows * row_bytes), cudaMemcpyDefault, st);
+      else
+        e = cudaMemcpy2DAsync(d, size_t(stage_stride_bytes), s, size_t(peer_stride_bytes), size_t(row_bytes),
+                              size_t(rows), cudaMemcpyDefault, st);
+      if (e != cudaSuccess) return cuda_fail(e, "stage_bank_range copy");
+    }
+  }
   return DUAL_OK;
 }
 

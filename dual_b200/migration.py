@@ -165,6 +165,21 @@ class TierManager:
         self.migrations: List[dict] = []
         self.restorations: List[dict] = []
 
+    def remote_row_ranges(self, num_banks: int) -> List[Tuple[int, int]]:
+        """Per supplier bank, the ``[begin, end)`` physical rows that hold committed remote positions
+        (host mirror, no device read; ``(0, 0)`` for a bank with none): what ``LayerStager`` copies
+        in its ``"range"`` mode.  Global id ``g`` -> bank ``g % n``, row ``g // n``, the split of the
+        reference's staging audit (``peer/staging.py:21-22``); the reference copies whole banks."""
+        if num_banks < 1:
+            raise ValueError("num_banks must be >= 1")
+        lo = [None] * num_banks
+        hi = [0] * num_banks
+        for g in self.remote_positions.values():
+            b, r = g % num_banks, g // num_banks
+            lo[b] = r if lo[b] is None else min(lo[b], r)
+            hi[b] = max(hi[b], r + 1)
+        return [(0, 0) if lo[b] is None else (lo[b], hi[b]) for b in range(num_banks)]
+
     def local_active(self) -> int:
         return self.local_capacity - self.allocator.available_size()
 

@@ -207,6 +207,62 @@ def migrate_copy(local_planes: torch.Tensor, remote_planes: torch.Tensor, num_pl
         status.data_ptr(), int(max_ctas), dev, _stream(source.device)))
 
 
+def stage_remote_rows(peer_k: Sequence[torch.Tensor], peer_v: Sequence[torch.Tensor],
+                      stage_k: Sequence[torch.Tensor], stage_v: Sequence[torch.Tensor],
+                      unified_indices: torch.Tensor, local_capacity: int, status: torch.Tensor,
+                      num_indices: Optional[int] = None, max_ctas: int = 0) -> None:
+    """Copy the supplier rows the index list names (both planes) into the same rows of local stage
+    buffers, which then replace the banks in ``tiered_append`` with the index list unchanged."""
+    _check(unified_indices.dtype == torch.int32 and unified_indices.is_contiguous(), "indices must be contiguous int32")
+    _check(status.dtype in (torch.int32, torch.uint32) and status.numel() >= 1, "status must be a 32-bit word")
+    n, slots, ps, ss = _stage_shapes(peer_k, peer_v, stage_k, stage_v, unified_indices.device)
+    count = unified_indices.numel() if num_indices is None else int(num_indices)
+    _check(0 <= count <= unified_indices.numel(), "num_indices out of range")
+    lib = _lib.load()
+    _lib.check(lib.dual_stage_remote_rows(
+        _ptrs(peer_k), _ptrs(peer_v), _ptrs(stage_k), _ptrs(stage_v), n, ps, ss, slots, SLOT_BYTES,
+        unified_indices.data_ptr(), count, int(local_capacity), status.data_ptr(), int(max_ctas),
+        _dev(unified_indices), _stream(unified_indices.device)))
+
+
+def stage_bank_range(peer_k: Sequence[torch.Tensor], peer_v: Sequence[torch.Tensor],
+                     stage_k: Sequence[torch.Tensor], stage_v: Sequence[torch.Tensor],
+                     row_ranges: Sequence[Sequence[int]], streams: Sequence[torch.cuda.Stream]) -> None:
+    """Copy rows [begin, end) of both planes of every bank into the same rows of its stage buffers
+    on the copy engines, bank b on ``streams[b]`` (no SM work)."""
+    n, slots, ps, ss = _stage_shapes(peer_k, peer_v, stage_k, stage_v, stage_k[0].device)
+    _check(len(row_ranges) == n and len(streams) == n, "need one row range and one stream per bank")
+    begin = (C.c_int64 * n)(*[int(r[0]) for r in row_ranges])
+    end = (C.c_int64 * n)(*[int(r[1]) for r in row_ranges])
+    handles = (C.c_void_p * n)(*[s.cuda_stream for s in streams])
+    lib = _lib.load()
+    _lib.check(lib.dual_stage_bank_range(
+        _ptrs(peer_k), _ptrs(peer_v), _ptrs(stage_k), _ptrs(stage_v), n, ps, ss, slots, SLOT_BYTES, begin, end,
+        handles, _dev(stage_k[0])))
+
+
+def _ptrs(ts: Sequence[torch.Tensor]):
+    return (C.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+
+
+def _stage_shapes(peer_k, peer_v, stage_k, stage_v, device):
+    """(banks, rows, bank stride, stage stride) after checking every bank / stage plane."""
+    n = len(peer_k)
+    _check(n >= 1 and len(peer_v) == n and len(stage_k) == n and len(stage_v) == n,
+           "need one (k, v) bank and one (k, v) stage buffer per supplier")
+    slots = peer_k[0].shape[0]
+    ps = _pool_stride(peer_k[0], "peer_k0")
+    ss = _pool_stride(stage_k[0], "stage_k0")
+    for i in range(n):
+        for t, name, stride in ((peer_k[i], "peer_k", ps), (peer_v[i], "peer_v", ps), (stage_k[i], "stage_k", ss),
+                                (stage_v[i], "stage_v", ss)):
+            _check(t.shape[0] == slots and _pool_stride(t, f"{name}{i}") == stride,
+                   f"{name}{i}: every bank and stage buffer needs the same rows and stride")
+        _check(stage_k[i].device == device and stage_v[i].device == device,
+               "stage buffers must be on the index list's device")
+    return n, slots, ps, ss
+
+
 def debug_inject(mask: int) -> None:
     """Test hook: DUAL_INJECT_* bits for the following launches (0 disables; see dual_b200.h)."""
     _lib.check(_lib.load().dual_debug_inject(int(mask)))

@@ -172,6 +172,36 @@ int dual_migrate_copy(const int64_t* local_planes, const int64_t* remote_planes,
                       int reverse, int64_t row_bytes, int64_t local_slots, int64_t remote_slots,
                       uint32_t* status, int max_ctas, int device, void* stream);
 
+/* ------------------------------------------------------------ staging ---
+ * Replaces LayerStager.launch (peer/staging.py:27-38), which copies every supplier bank's whole
+ * layer into a local one-layer buffer before the prefill of that layer reads it
+ * (peer/prefill_backend.py:33), selectively: for every entry p of unified_indices[0, num_indices)
+ * with p > local_capacity (global remote id g = p - local_capacity - 1), copies row g / num_banks
+ * of both planes of bank g % num_banks (peer_k[b], peer_v[b]: one layer's planes, bank_slots rows
+ * at peer_stride_bytes) to the same row of stage_k[b] / stage_v[b] (local buffers, bank_slots rows
+ * at stage_stride_bytes).  Local entries are skipped; rows no entry names are left untouched.  The
+ * stage buffers then replace the banks in dual_tiered_append (or dual_tiered_decode) with the same
+ * index list.  row_bytes (2048 for 8 kv heads x 128 x bf16) and the strides are multiples of 16.
+ * A remote id beyond the banks is skipped and records DUAL_STATUS_BAD_REMOTE_SLOT.  max_ctas bounds
+ * the grid (0 = one single-warp CTA per 32 entries). */
+int dual_stage_remote_rows(const void* const* peer_k, const void* const* peer_v, void* const* stage_k,
+                           void* const* stage_v, int num_banks, int64_t peer_stride_bytes,
+                           int64_t stage_stride_bytes, int64_t bank_slots, int64_t row_bytes,
+                           const int32_t* unified_indices, int64_t num_indices, int64_t local_capacity,
+                           uint32_t* status, int max_ctas, int device, void* stream);
+
+/* Row-range staging on the copy engines, the reference's form (LayerStager.launch copies each
+ * donor's whole layer with one copy per donor on its own stream, peer/staging.py:27-38): for each
+ * bank b with row_begin[b] < row_end[b], copies rows [row_begin[b], row_end[b]) of both planes from
+ * peer_k/peer_v[b] to the same rows of stage_k/stage_v[b] -- one cudaMemcpyAsync per plane when
+ * both strides equal row_bytes, else one cudaMemcpy2DAsync -- on streams[b] (host array of
+ * num_banks stream handles; NULL entries mean the legacy default stream).  No SM work, so it
+ * overlaps a running attention kernel.  Ranges must lie within [0, bank_slots]. */
+int dual_stage_bank_range(const void* const* peer_k, const void* const* peer_v, void* const* stage_k,
+                          void* const* stage_v, int num_banks, int64_t peer_stride_bytes,
+                          int64_t stage_stride_bytes, int64_t bank_slots, int64_t row_bytes,
+                          const int64_t* row_begin, const int64_t* row_end, void* const* streams, int device);
+
 /* ------------------------------------------------------ fault injection ---
  * Test hook with no counterpart in the reference (whose failure handling is fail-fast asserts):
  * makes a device-side wait run out without faulting the GPU, so tests can check that the

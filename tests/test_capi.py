@@ -45,6 +45,22 @@ def test_argument_errors_are_codes_not_crashes():
         _lib.check(lib.dual_write_prefill_layout(None, None, 1, 1, None, None, None, None, None, 1, 3, 5, None, -1, None))
 
 
+def test_stage_arguments_are_checked_before_any_launch():
+    lib = _lib.load()
+    assert lib.dual_stage_remote_rows(None, None, None, None, 1, 2048, 2048, 4, 2048, None, 0, 10, None, 0, -1,
+                                      None) == 0
+    arr = (C.c_void_p * 1)(16)
+    rc = lib.dual_stage_remote_rows(arr, arr, arr, arr, 0, 2048, 2048, 4, 2048, 16, 8, 10, 16, 0, -1, None)
+    assert rc == 1 and b"num_banks" in lib.dual_last_error()
+    rc = lib.dual_stage_remote_rows(arr, arr, arr, arr, 1, 2048, 2048, 4, 2047, 16, 8, 10, 16, 0, -1, None)
+    assert rc == 1 and b"row_bytes" in lib.dual_last_error()
+    rc = lib.dual_stage_remote_rows(arr, arr, arr, arr, 1, 1024, 2048, 4, 2048, 16, 8, 10, 16, 0, -1, None)
+    assert rc == 1 and b"strides" in lib.dual_last_error()
+    bad = (C.c_void_p * 1)(24)
+    rc = lib.dual_stage_remote_rows(arr, arr, bad, arr, 1, 2048, 2048, 4, 2048, 16, 8, 10, 16, 0, -1, None)
+    assert rc == 1 and b"aligned" in lib.dual_last_error()
+
+
 def test_fault_injection_mask_is_validated():
     """The test-only injection hook accepts its known bit and 0, refuses anything else (no GPU)."""
     lib = _lib.load()

@@ -87,6 +87,26 @@ def test_fifo_migration_preserves_every_position_and_invariants():
         assert np.array_equal(after[k][0], v[0]) and np.array_equal(after[k][1], v[1]), k
 
 
+def test_remote_row_ranges_cover_every_committed_remote_position():
+    m, pools = _manager()
+    assert m.remote_row_ranges(3) == [(0, 0)] * 3
+    for rid in range(4):
+        m.begin_forward()
+        m.append(rid, 40)
+    m.begin_forward()
+    m.submit(needed=0, asynchronous=True)
+    assert m.remote_row_ranges(3) == [(0, 0)] * 3  # nothing committed yet
+    m.commit()
+    ranges = m.remote_row_ranges(3)
+    for (rid, pos), g in m.remote_positions.items():
+        lo, hi = ranges[g % 3]
+        assert lo <= g // 3 < hi
+        assert int(m.tier[rid, pos]) == 1 and int(m.slot[rid, pos]) == g
+    assert sum(hi - lo for lo, hi in ranges) >= len(m.remote_positions)
+    with pytest.raises(ValueError):
+        m.remote_row_ranges(0)
+
+
 def test_strict_bound_is_never_crossed():
     m, pools = _manager(local_cap=400, tokens=2048, ctx=400)
     m.begin_forward()
