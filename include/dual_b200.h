@@ -105,8 +105,9 @@ int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_
 
 /* ------------------------------------------------------ tiered append ---
  * Replaces the tiered FA2 batch-prefill module on the append path (run hook
- * peer/prefill_backend.py:25-42, module peer/flashinfer_peer.py:105-142) and the per-layer
- * staging of supplier banks (peer/staging.py): remote rows are read in place.
+ * peer/prefill_backend.py:25-42, module peer/flashinfer_peer.py:105-142).  The banks passed as
+ * peer_k / peer_v are read wherever they live: the suppliers' memory (peer loads) or local stage
+ * buffers filled by dual_stage_bank_range / dual_stage_remote_rows.
  * Semantics of FlashInfer's BatchPrefillWithPagedKVCacheWrapper (page_size 1): request b has
  * qo_indptr[b+1]-qo_indptr[b] query tokens and kv_indptr[b+1]-kv_indptr[b] list entries; with
  * causal != 0 query token i sees entry j iff j < L_b - q_b (history, any order) or
