@@ -874,7 +874,8 @@ def run_append(args):
     if not args.no_cpu_baseline:
         cpu = append_cpu_baseline(lengths, qlens, flops)
     print(json.dumps({"metric": "causal append attention time per layer", "value": round(ms, 4), "unit": "ms",
-                      "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+                      "n_gpus": len({str(dev)} | {str(o) for o in owners}), "steps": args.steps,
+                      "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
                       "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                       "data": "synthetic", "tflops": round(tf, 1),
                       "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
