@@ -199,7 +199,11 @@ class DecodeWorkload:
 
 class E2E:
     """Same metric through the public wrapper API with host buffers: per step H2D of the step's
-    queries (pinned), plan(), the packer, 36 x wrapper.run, D2H of the outputs (pinned)."""
+    queries (pinned), plan(), the packer, 36 x wrapper.run, D2H of the outputs (pinned).  The copies
+    are pipelined by layer inside the step, as a serving process would issue them: layer l's queries
+    go up on an H2D stream and its output comes back on a D2H stream as soon as layer l is done, so
+    only layer 0's upload and layer 35's download are exposed; the step ends when every output of
+    the step is in host memory."""
 
     def __init__(self, w: DecodeWorkload):
         from dual_b200.wrapper import BatchDecodeWithPagedKVCacheWrapper
@@ -211,16 +215,30 @@ class E2E:
         self.wrapper = BatchDecodeWithPagedKVCacheWrapper(torch.empty(64 << 20, dtype=torch.uint8, device=w.device),
                                                           "NHD", use_tensor_cores=True)
         self.last = torch.ones(w.B, dtype=torch.int32)
+        self.h2d = torch.cuda.Stream(w.device)
+        self.d2h = torch.cuda.Stream(w.device)
+        self.q_ready = [torch.cuda.Event() for _ in range(w.layers)]
+        self.out_ready = [torch.cuda.Event() for _ in range(w.layers)]
 
     def step(self):
         w = self.w
-        self.q_dev.copy_(self.q_host, non_blocking=True)
+        cur = torch.cuda.current_stream(w.device)
+        self.h2d.wait_stream(cur)  # the previous step's layers are done with q_dev
+        with torch.cuda.stream(self.h2d):
+            for i in range(w.layers):
+                self.q_dev[i].copy_(self.q_host[i], non_blocking=True)
+                self.q_ready[i].record(self.h2d)
         w.ops.pack_read_order(w.tier, w.slot, w.req, w.seq, w.C, 5, 32, w.indices, status=w.status)
         self.wrapper.plan(self.indptr_host, w.indices, self.last, 32, 8, 128, 1, q_data_type=torch.bfloat16,
                           sm_scale=w.scale)
         for i in range(w.layers):
+            cur.wait_event(self.q_ready[i])
             self.wrapper.run(self.q_dev[i], (w.k[i], w.v[i]), out=w.out[i])
-        self.out_host.copy_(w.out, non_blocking=True)
+            self.out_ready[i].record(cur)
+            self.d2h.wait_event(self.out_ready[i])
+            with torch.cuda.stream(self.d2h):
+                self.out_host[i].copy_(w.out[i], non_blocking=True)
+        cur.wait_stream(self.d2h)  # the step ends when its outputs are in host memory
 
     def h2d_bytes(self):
         return self.q_host.numel() * 2 + self.indptr_host.numel() * 4
