@@ -61,6 +61,8 @@ SIGNATURES = {
         VP, VP, C.c_int64, C.c_int64, VP, VP, VP, VP, C.c_int, C.c_int64, C.c_int, C.c_int, VP, VP, VP, C.c_int, VP]),
     "dual_write_prefill_layout": (C.c_int, [
         VP, VP, C.c_int64, C.c_int64, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int, VP, C.c_int, VP]),
+    "dual_set_kv_buffer": (C.c_int, [
+        VP, VP, C.c_int64, C.c_int64, VP, C.c_int64, VP, C.c_int64, VP, C.c_int, C.c_int64, VP, C.c_int, VP]),
     "dual_migrate_copy": (C.c_int, [
         VP, VP, C.c_int, C.c_int, VP, VP, C.c_int64, C.c_int, C.c_int64, C.c_int64, C.c_int64, VP, C.c_int,
         C.c_int, VP]),

@@ -18,7 +18,7 @@ CSRC = PKG / "csrc"
 LIBDIR = PKG / "lib"
 LIBNAME = "libdual_b200.so"
 SUPPLIER = "dual_supplier"  # native KV-supplier process (supplier_service.cpp)
-SOURCES = ["capi.cu", "decode.cu", "decode_noalloc.cu", "pack.cu", "migrate.cu", "prefill.cu", "stage.cu"]
+SOURCES = ["capi.cu", "decode.cu", "decode_noalloc.cu", "pack.cu", "migrate.cu", "prefill.cu", "stage.cu", "kv_write.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

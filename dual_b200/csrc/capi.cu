@@ -8,6 +8,7 @@
 
 #include "dual_b200.h"
 #include "decode.cuh"
+#include "kv_write.cuh"
 #include "migrate.cuh"
 #include "pack.cuh"
 #include "prefill.cuh"
@@ -371,6 +372,40 @@ int dual_write_prefill_layout(int32_t* tier, int32_t* slot, int64_t table_rows, 
   p.status = status;
   cudaError_t e = dual::launch_write_layout(p, max_length, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "write_prefill_layout launch");
+  return DUAL_OK;
+}
+
+int dual_set_kv_buffer(void* k_local, void* v_local, int64_t local_stride_bytes, int64_t local_capacity,
+                       const void* k, int64_t k_stride_token, const void* v, int64_t v_stride_token,
+                       const void* locations, int loc_is_int64, int64_t n, uint32_t* status, int device,
+                       void* stream) {
+  g_last_error.clear();
+  if (n < 0) return fail(DUAL_EINVAL, "n must be >= 0");
+  if (n == 0) return DUAL_OK;
+  if (!k_local || !v_local || !k || !v || !locations || !status) return fail(DUAL_EINVAL, "null pointer argument");
+  const int64_t row = int64_t(dual::kNumKvHeads) * dual::kHeadDim * 2;
+  if (!aligned16(k_local) || !aligned16(v_local) || (local_stride_bytes & 15) || local_stride_bytes < row)
+    return fail(DUAL_EINVAL, "local pools must be 16-byte aligned with a slot stride >= 2048 B, multiple of 16");
+  if (!aligned16(k) || !aligned16(v) || (k_stride_token % 8) || (v_stride_token % 8) ||
+      k_stride_token < row / 2 || v_stride_token < row / 2)
+    return fail(DUAL_EINVAL, "k/v must be 16-byte aligned with token strides >= 1024 elements, multiples of 8");
+  if (local_capacity < 0) return fail(DUAL_EINVAL, "local_capacity must be >= 0");
+  if (int rc = set_device(device)) return rc;
+  dual::KvWriteParams p{};
+  p.k_local = static_cast<char*>(k_local);
+  p.v_local = static_cast<char*>(v_local);
+  p.local_stride = local_stride_bytes;
+  p.capacity = local_capacity;
+  p.k = static_cast<const char*>(k);
+  p.v = static_cast<const char*>(v);
+  p.k_stride = k_stride_token * 2;
+  p.v_stride = v_stride_token * 2;
+  p.loc64 = loc_is_int64 ? static_cast<const int64_t*>(locations) : nullptr;
+  p.loc32 = loc_is_int64 ? nullptr : static_cast<const int32_t*>(locations);
+  p.n = n;
+  p.status = status;
+  cudaError_t e = dual::launch_set_kv_buffer(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "set_kv_buffer launch");
   return DUAL_OK;
 }
 

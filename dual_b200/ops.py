@@ -189,6 +189,26 @@ def write_prefill_layout(tier: torch.Tensor, slot: torch.Tensor, req_pool_indice
         _stream(tier.device)))
 
 
+def set_kv_buffer(k_local: torch.Tensor, v_local: torch.Tensor, locations: torch.Tensor, k: torch.Tensor,
+                  v: torch.Tensor, status: torch.Tensor) -> None:
+    """New tokens' K / V rows ``[n, 8, 128]`` (token stride free) into local slots ``locations``
+    (SGLang ``out_cache_loc``, int64 or int32) of one layer's pools; bad slots are skipped and recorded."""
+    ls = _pool_stride(k_local, "k_local")
+    _check(_pool_stride(v_local, "v_local") == ls, "k/v local pools must share a slot stride")
+    n = locations.numel()
+    for t, name in ((k, "k"), (v, "v")):
+        _check(t.dtype == torch.bfloat16 and t.dim() == 3 and tuple(t.shape[1:]) == (NUM_KV_HEADS, HEAD_DIM)
+               and t.stride(2) == 1 and t.stride(1) == HEAD_DIM and t.shape[0] == n,
+               f"{name} must be bf16 [n, 8, 128] with heads x dims contiguous")
+    _check(locations.dtype in (torch.int64, torch.int32) and locations.is_contiguous(), "locations must be int64/int32")
+    _check(status.dtype in (torch.int32, torch.uint32) and status.numel() >= 1, "status must be a 32-bit word")
+    lib = _lib.load()
+    _lib.check(lib.dual_set_kv_buffer(
+        k_local.data_ptr(), v_local.data_ptr(), ls, k_local.shape[0] - 1, k.data_ptr(), k.stride(0), v.data_ptr(),
+        v.stride(0), locations.data_ptr(), int(locations.dtype == torch.int64), n, status.data_ptr(), _dev(k_local),
+        _stream(k_local.device)))
+
+
 def migrate_copy(local_planes: torch.Tensor, remote_planes: torch.Tensor, num_planes: int, num_banks: int,
                  source: torch.Tensor, target: torch.Tensor, reverse: bool, local_slots: int,
                  remote_slots: int, status: torch.Tensor, row_bytes: int = SLOT_BYTES, max_ctas: int = 0) -> None:

@@ -160,6 +160,18 @@ int dual_write_prefill_layout(int32_t* tier, int32_t* slot, int64_t table_rows, 
                               const void* locations, int loc_is_int64, int batch, int max_length,
                               uint32_t* status, int device, void* stream);
 
+/* Replaces SGLang's MHATokenToKVPool.set_kv_buffer as the reference calls it before every tiered
+ * attention launch (V/nvlink_prefill_timing/backend.py:34,42): new positions are always local
+ * (tier 0), so for i < n the K and V rows of token i (8 kv heads x 128 bf16, heads x dims
+ * contiguous, token strides k_stride_token / v_stride_token in elements) are copied to slot
+ * locations[i] of k_local / v_local (slot stride local_stride_bytes).  locations are int64 (SGLang
+ * out_cache_loc) when loc_is_int64, else int32.  A slot outside [0, local_capacity] (0 is SGLang's
+ * dummy slot) is skipped and records DUAL_STATUS_BAD_LOCAL_SLOT.  Bit-exact. */
+int dual_set_kv_buffer(void* k_local, void* v_local, int64_t local_stride_bytes, int64_t local_capacity,
+                       const void* k, int64_t k_stride_token, const void* v, int64_t v_stride_token,
+                       const void* locations, int loc_is_int64, int64_t n, uint32_t* status, int device,
+                       void* stream);
+
 /* ------------------------------------------------------------- migration ---
  * Replaces Triton fused_copy._copy / copy_pages / restore (peer/fused_copy.py:6-33):
  * for each i < n and each plane: reverse==0 copies local slot source[i] to remote id

@@ -61,6 +61,17 @@ def test_stage_arguments_are_checked_before_any_launch():
     assert rc == 1 and b"aligned" in lib.dual_last_error()
 
 
+def test_kv_writer_arguments_are_checked_before_any_launch():
+    lib = _lib.load()
+    assert lib.dual_set_kv_buffer(None, None, 2048, 10, None, 1024, None, 1024, None, 1, 0, None, -1, None) == 0
+    rc = lib.dual_set_kv_buffer(16, 16, 2048, 10, 16, 1000, 16, 1024, 16, 1, 4, 16, -1, None)
+    assert rc == 1 and b"token strides" in lib.dual_last_error()
+    rc = lib.dual_set_kv_buffer(16, 16, 1024, 10, 16, 1024, 16, 1024, 16, 1, 4, 16, -1, None)
+    assert rc == 1 and b"slot stride" in lib.dual_last_error()
+    rc = lib.dual_set_kv_buffer(None, 16, 2048, 10, 16, 1024, 16, 1024, 16, 1, 4, 16, -1, None)
+    assert rc == 1 and b"null" in lib.dual_last_error()
+
+
 def test_fault_injection_mask_is_validated():
     """The test-only injection hook accepts its known bit and 0, refuses anything else (no GPU)."""
     lib = _lib.load()

@@ -1,7 +1,8 @@
 """A small serving loop through the public pieces, driven the way the reference's backend drives them
 (peer/backend.py, peer/prefill_backend.py, peer/policy.py, peer/staging.py): a prefill of three
-requests; FIFO migration of their oldest positions to two supplier banks (TierManager +
-CudaCopier), launched early and left in flight across an extend forward; a second extend whose
+requests (K/V written by the native KV writer); FIFO migration of their oldest positions to two
+supplier banks (TierManager + CudaCopier), launched early and left in flight across an extend
+forward; a second extend whose
 history is partly remote, read both in place and through the LayerStager (copy-engine ranges from
 TierManager.remote_row_ranges); then a decode step.  Every attention output is checked against the
 fp32 oracle over the logical K/V the loop wrote, the staged and in-place appends are bit-identical,
@@ -44,13 +45,16 @@ class Loop:
                         for _ in range(LAYERS)]
 
     def write(self, rid, n):
+        """A forward's new positions: local slots from the manager, K/V written by the native writer
+        (SGLang's set_kv_buffer in the reference) from a fused qkv buffer, as the model would."""
         start = self.m.live.get(rid, 0)
         s = torch.tensor(self.m.append(rid, n), dtype=torch.long, device=self.dev)
         for layer in range(LAYERS):
-            for plane in range(2):
-                rows = torch.empty((n, 8, 128), dtype=torch.bfloat16, device=self.dev).normal_(generator=self.g)
-                self.kv[layer][plane][s] = rows
-                self.logical[layer][plane][rid, start:start + n] = rows
+            qkv = torch.empty((n, 6144), dtype=torch.bfloat16, device=self.dev).normal_(generator=self.g)
+            k, v = qkv[:, 4096:5120].view(n, 8, 128), qkv[:, 5120:].view(n, 8, 128)
+            ops.set_kv_buffer(self.kv[layer][0], self.kv[layer][1], s, k, v, self.status)
+            self.logical[layer][0][rid, start:start + n] = k
+            self.logical[layer][1][rid, start:start + n] = v
 
     def full_list(self, rids, lengths, prefixes=None):
         d = self.dev
