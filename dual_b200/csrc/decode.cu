@@ -46,6 +46,8 @@ __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+constexpr float kDecodeRescale = 8.0f;  // log2 units
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __grid_constant__ TieredDecodeParams p) {
   constexpr int NS = Cfg::NS, TILE = Cfg::TILE, CONS = Cfg::CONSUMERS;
@@ -241,19 +243,27 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __
       float tmax = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
       tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
       tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-      const float m_new = fmaxf(m_run, tmax);
-      const float alpha = fast_exp2(m_run - m_new);
+      // Lazy rescaling: the reference point m_run moves (and O, d are rescaled) only when the tile
+      // max exceeds it by more than 2^kDecodeRescale, so P <= 256 in between; the partial state
+      // (O, m, d) stays exact because O and d share the reference point.  Rescaling every tile
+      // was 64 multiplies per lane per 16 tokens.
+      float alpha = 1.f;
+      if (tmax > m_run + kDecodeRescale) {
+        alpha = fast_exp2(m_run - tmax);  // 0 on a segment's first tile
+        m_run = tmax;
+      }
       float pr[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) pr[e] = fast_exp2(x[e] - m_new);
+      for (int e = 0; e < 4; ++e) pr[e] = fast_exp2(x[e] - m_run);
       d_run = d_run * alpha + (pr[0] + pr[1]) + (pr[2] + pr[3]);
-      m_run = m_new;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-      for (int nt = 0; nt < 16; ++nt) {
-        o[nt][0] *= alpha;
-        o[nt][1] *= alpha;
-        o[nt][2] *= alpha;
-        o[nt][3] *= alpha;
+        for (int nt = 0; nt < 16; ++nt) {
+          o[nt][0] *= alpha;
+          o[nt][1] *= alpha;
+          o[nt][2] *= alpha;
+          o[nt][3] *= alpha;
+        }
       }
       // P as a hi + lo pair of bf16 values, keeping P's bf16 rounding out of the output: hi feeds
       // MMA rows g (the 4 query heads), lo feeds the otherwise idle rows g + 8 of the same MMA;
