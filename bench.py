@@ -12,9 +12,11 @@ flush is needed between iterations.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dual|reference] [--workload W]
 
-Workloads: config2 (default), small; config3, config5, tiered-small (a compute GPU + a supplier GPU;
-under torchrun N/2 such pairs); config4, append-small, append-mid (causal append); migration;
-fi-<workload> times native FlashInfer FA2 on the same inputs (the number to beat).
+Workloads: config2 (default), small; config3, config5, tiered-small, and config3-local / config3-r12
+(config 3's batch with no remote rows / twice its remote share) (a compute GPU + a supplier GPU;
+under torchrun N/2 such pairs); config4, append-small, append-mid (causal append; --stage range|rows
+stages the supplier rows per layer); migration; fi-<workload> times native FlashInfer FA2 on the
+same inputs (the number to beat).
 
 Under torchrun (N > 1) every rank serves its own independent batch (decode
 shards by request; no collective on the data path): scaling "weak".
@@ -51,6 +53,9 @@ WORKLOADS = {
 # name: (batch, Lmin, Lmax, remote/local ratio, remote placement, RN, TN, layers resident, migrate)
 TIERED = {
     "config3": (128, 2048, 32768, 0.0599, "tail", 8, 128, 6, False),
+    # config 3 at equal batch with no remote rows and with twice its remote share (all-local comparison)
+    "config3-local": (128, 2048, 32768, 0.0, "tail", 8, 128, 6, False),
+    "config3-r12": (128, 2048, 32768, 0.12, "tail", 8, 128, 6, False),
     "config5": (128, 4096, 32768, 0.1797, "prefix", 5, 32, 6, True),
     # profiling case: config-5 ratios and read order, 16 requests, 2 resident layers (~3 GB on the device)
     "tiered-small": (16, 4096, 32768, 0.1797, "prefix", 5, 32, 2, False),
@@ -427,7 +432,7 @@ class TieredWorkload:
         self.mig_tokens = 2048 if migrate else 0
         n_bg = 4 * self.mig_tokens  # background (not decoded) positions that migrate each step
         C = int(self.local.sum()) + n_bg
-        R_cap = self.R + n_bg
+        R_cap = max(1, self.R + n_bg)  # a one-row bank when nothing is remote
         self.C, self.R_cap = C, R_cap
         g = torch.Generator(device=self.d0).manual_seed(seed)
         self.k = [torch.empty((C + 1, 8, 128), dtype=torch.bfloat16, device=self.d0) for _ in range(layers)]
