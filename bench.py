@@ -127,7 +127,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, watts = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.splitlines():
             f = [x.strip() for x in line.split(",")]
@@ -138,12 +138,17 @@ class ClockSampler:
                 mx = float(f[1])
             except ValueError:
                 continue
+            try:
+                watts.append(float(f[2]))
+            except ValueError:
+                pass
             for name, val in zip(names, f[3:7]):
                 if val.lower() == "active":
                     reasons.add(name)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "power_w": statistics.median(watts) if watts else None}
 
 
 # ------------------------------------------------------------------- dual arm
