@@ -228,3 +228,49 @@ def test_stale_work_list_is_a_status_error_not_a_fault():
     ops.tiered_append(q, k, v, total, [], [], qo2, kv2, idx, True, 128 ** -0.5, work, out, lse, status)
     torch.cuda.synchronize()
     assert int(status.item()) & 0x10  # DUAL_STATUS_BAD_LENGTH
+
+
+def test_append_eight_supplier_banks():
+    case = _random_batch(41, B=4, banks=8)
+    k, v, pk, pv, tier, slot = _dev(case)
+    full, _ = _full_list(tier, slot, case.requests, case.lengths, case.prefixes, case.local_capacity)
+    out, lse, st = _append(case.q, k, v, pk, pv, case.qlens, case.lengths, full, case.local_capacity)
+    assert st == 0
+    ref, ref_lse = OA.tiered_attention(case.q, case.k_local, case.v_local, case.peer_k, case.peer_v, case.tier,
+                                       case.slot, case.requests, case.lengths, case.qlens, case.prefixes)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
+
+
+def test_append_rescales_when_the_max_keeps_growing():
+    """History rows whose scores climb along the list: the running maximum moves past the lazy
+    rescale threshold again and again, and the output in TMEM is rescaled in place each time."""
+    g = torch.Generator().manual_seed(5)
+    prefixes, qlens = [3000, 700], [40, 130]
+    lengths = [p + q for p, q in zip(prefixes, qlens)]
+    total = sum(lengths)
+    # queries of kv head h all lean towards one direction u_h; the history's keys climb along u_h
+    direction = torch.randn((8, 128), generator=g)
+    direction = direction / direction.norm(dim=-1, keepdim=True)
+    q = direction.repeat_interleave(4, 0)[None] + 0.5 * torch.randn((sum(qlens), 32, 128), generator=g) / 128 ** 0.5
+    q = q / q.norm(dim=-1, keepdim=True)
+    k = torch.randn((total + 1, 8, 128), generator=g) * 0.3
+    v = torch.randn((total + 1, 8, 128), generator=g).to(torch.bfloat16)
+    slots, off = [], 1
+    for L in lengths:
+        ramp = torch.linspace(0.0, 330.0, L)
+        k[off:off + L] += ramp[:, None, None] * direction[None]
+        slots.append(torch.arange(off, off + L, dtype=torch.int32))
+        off += L
+    q, k = q.to(torch.bfloat16), k.to(torch.bfloat16)
+    tier = torch.zeros((2, max(lengths)), dtype=torch.int32)
+    slot = torch.zeros_like(tier)
+    for b, L in enumerate(lengths):
+        slot[b, :L] = slots[b]
+    d = torch.device(DEV)
+    full, _ = _full_list(tier.to(d), slot.to(d), [0, 1], lengths, prefixes, total)
+    out, lse, st = _append(q, k.to(d), v.to(d), [], [], qlens, lengths, full, total)
+    assert st == 0
+    ref, ref_lse = OA.tiered_attention(q, k, v, [], [], tier, slot, [0, 1], lengths, qlens, prefixes)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)

@@ -187,3 +187,49 @@ def test_decode_long_contexts_against_oracle():
     ref, ref_lse = OA.decode_from_indices(q, k, v, [], [], indptr.tolist(), perm, pool)
     torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
     torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
+
+
+def test_decode_eight_supplier_banks():
+    """The most supplier banks the ABI takes (8): striping g % 8 over every case's remote rows."""
+    for case in C.all_cases(banks=8):
+        dev = to_dev(case)
+        indptr, idx, st = pack_decode(dev, case.requests, case.lengths, case.local_capacity)
+        out, lse, ws = decode(case.decode_q(), dev, indptr, idx, case.local_capacity)
+        ref, ref_lse = OA.decode_from_indices(case.decode_q(), case.k_local, case.v_local, case.peer_k, case.peer_v,
+                                              indptr.cpu().tolist(), idx.cpu(), case.local_capacity)
+        torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL, msg=case.name)
+        torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL, msg=case.name)
+        assert _status(ws) == 0 and int(st.item()) == 0
+
+
+def _growing_scores(lengths, pool, seed):
+    """K rows whose scores with q climb along the list (by ~40 in the log2 domain over a request),
+    so the running maximum keeps moving past the lazy-rescale threshold (2^8) inside a segment."""
+    g = torch.Generator().manual_seed(seed)
+    B = len(lengths)
+    q = torch.randn((B, 32, 128), generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    k = torch.randn((pool + 1, 8, 128), generator=g) * 0.3
+    v = torch.randn((pool + 1, 8, 128), generator=g).to(torch.bfloat16)
+    perm = (torch.randperm(pool, generator=g) + 1)[: sum(lengths)]
+    off = 0
+    for b, L in enumerate(lengths):
+        ramp = torch.linspace(0.0, 330.0, L)  # x 128^-0.5 x log2(e) ~ 42 in the log2 domain
+        direction = q[b].float().view(8, 4, 128).mean(dim=1)  # shared by the GQA group of each kv head
+        k[perm[off:off + L]] += ramp[:, None, None] * direction[None] / direction.norm(dim=-1, keepdim=True)[None]
+        off += L
+    return q, k.to(torch.bfloat16), v, perm.int()
+
+
+def test_decode_rescales_when_the_max_keeps_growing():
+    lengths = [5000, 300, 17, 2600]
+    pool = sum(lengths) + 10
+    q, k, v, perm = _growing_scores(lengths, pool, 3)
+    indptr = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32)
+    dev = dict(k_local=k.to(DEV), v_local=v.to(DEV), peer_k=[], peer_v=[])
+    for num_ctas in (0, 7):
+        out, lse, ws = decode(q, dev, indptr.to(DEV), perm.to(DEV), pool, num_ctas=num_ctas)
+        ref, ref_lse = OA.decode_from_indices(q, k, v, [], [], indptr.tolist(), perm, pool)
+        torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+        torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
+        assert _status(ws) == 0
