@@ -274,3 +274,31 @@ def test_append_rescales_when_the_max_keeps_growing():
     ref, ref_lse = OA.tiered_attention(q, k, v, [], [], tier, slot, [0, 1], lengths, qlens, prefixes)
     torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
     torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
+
+
+def test_append_strided_views_and_other_scale():
+    """q as a view of a fused qkv projection and out inside a wider buffer, scale 0.07."""
+    case = _random_batch(43, B=3)
+    k, v, pk, pv, tier, slot = _dev(case)
+    full, _ = _full_list(tier, slot, case.requests, case.lengths, case.prefixes, case.local_capacity)
+    d = torch.device(DEV)
+    n = case.q.shape[0]
+    qkv = torch.zeros((n, 6144), dtype=torch.bfloat16, device=d)
+    qkv[:, :4096] = case.q.to(d).view(n, 4096)
+    q = qkv[:, :4096].view(n, 32, 128)
+    wide = torch.full((n, 40, 128), 3.0, dtype=torch.bfloat16, device=d)
+    out = wide[:, 8:]
+    qo = np.concatenate([[0], np.cumsum(case.qlens)]).astype(np.int32)
+    kv = np.concatenate([[0], np.cumsum(case.lengths)]).astype(np.int32)
+    work = ops.append_plan(qo, kv, True).to(d)
+    lse = torch.empty((n, 32), dtype=torch.float32, device=d)
+    status = torch.zeros(1, dtype=torch.int32, device=d)
+    ops.tiered_append(q, k, v, case.local_capacity, pk, pv, torch.from_numpy(qo).to(d), torch.from_numpy(kv).to(d),
+                      full, True, 0.07, work, out, lse, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref, ref_lse = OA.tiered_attention(case.q, case.k_local, case.v_local, case.peer_k, case.peer_v, case.tier,
+                                       case.slot, case.requests, case.lengths, case.qlens, case.prefixes, sm_scale=0.07)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
+    assert bool((wide[:, :8] == 3.0).all())

@@ -233,3 +233,27 @@ def test_decode_rescales_when_the_max_keeps_growing():
         torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
         torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL)
         assert _status(ws) == 0
+
+
+def test_decode_strided_views_and_other_scale():
+    """q as a view of a fused qkv projection (token stride 6144), out as a view into a wider buffer,
+    a scale other than 128^-0.5 and no LSE: the strides go through the ABI as given."""
+    case = C.config1(banks=3)
+    dev = to_dev(case)
+    indptr, idx, _ = pack_decode(dev, case.requests, case.lengths, case.local_capacity)
+    B = len(case.lengths)
+    qkv = torch.zeros((B, 6144), dtype=torch.bfloat16, device=DEV)
+    qkv[:, :4096] = case.decode_q().to(DEV).view(B, 4096)
+    q = qkv[:, :4096].view(B, 32, 128)
+    wide = torch.full((B, 40, 128), 3.0, dtype=torch.bfloat16, device=DEV)
+    out = wide[:, 4:36]
+    ws = torch.zeros(ops.decode_workspace_size(B, ops.default_ctas(0)), dtype=torch.uint8, device=DEV)
+    scale = 0.05
+    ops.tiered_decode(q, dev["k_local"], dev["v_local"], case.local_capacity, dev["peer_k"], dev["peer_v"], indptr,
+                      idx, scale, out, None, ws)
+    torch.cuda.synchronize()
+    ref, _ = OA.decode_from_indices(case.decode_q(), case.k_local, case.v_local, case.peer_k, case.peer_v,
+                                    indptr.cpu().tolist(), idx.cpu(), case.local_capacity, sm_scale=scale)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+    assert bool((wide[:, :4] == 3.0).all()) and bool((wide[:, 36:] == 3.0).all())  # nothing outside the view
+    assert _status(ws) == 0
