@@ -11,7 +11,7 @@ TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
 """
 from __future__ import annotations
 
-from typing import List, Sequence
+from typing import Sequence
 
 import numpy as np
 

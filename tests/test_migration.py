@@ -6,7 +6,6 @@ import pytest
 import torch
 
 from dual_b200.migration import LocalAllocator, TierManager, limit_pages
-from oracle import attention as OA
 from oracle import copy as OC
 from oracle import policy as OP
 

@@ -4,7 +4,6 @@ given row ranges, bit-exact, nothing else written; the append kernel over the st
 bit-identical outputs to the append over the banks; the LayerStager in both modes over a
 multi-layer RemoteBank matches per-layer in-place reads; a remote id beyond the banks is skipped
 and reported."""
-import numpy as np
 import pytest
 import torch
 
