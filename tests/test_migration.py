@@ -106,6 +106,23 @@ def test_remote_row_ranges_cover_every_committed_remote_position():
         m.remote_row_ranges(0)
 
 
+def test_remote_row_ranges_follow_releases():
+    """After the requests that own every remote row are released, no bank has a range left to stage."""
+    m, pools = _manager()
+    for rid in range(4):
+        m.begin_forward()
+        m.append(rid, 40)
+    m.begin_forward()
+    m.submit(needed=0, asynchronous=True)
+    m.commit()
+    owners = {rid for rid, _ in m.remote_positions}
+    assert owners and any(hi > lo for lo, hi in m.remote_row_ranges(3))
+    m.release(sorted(owners))
+    assert not m.remote_positions
+    assert m.remote_row_ranges(3) == [(0, 0)] * 3
+    m.audit()
+
+
 def test_strict_bound_is_never_crossed():
     m, pools = _manager(local_cap=400, tokens=2048, ctx=400)
     m.begin_forward()
