@@ -37,7 +37,7 @@ def _stale(target: Path) -> bool:
     if not target.exists():
         return True
     mtime = target.stat().st_mtime
-    deps = (list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.cpp"))
+    deps = (list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(CSRC.glob("*.cpp"))
             + [ROOT / "include" / "dual_b200.h"])
     return any(d.stat().st_mtime > mtime for d in deps if d.exists())
 

@@ -8,6 +8,7 @@
 
 #include "dual_b200.h"
 #include "decode.cuh"
+#include "device_guard.h"
 #include "kv_write.cuh"
 #include "migrate.cuh"
 #include "pack.cuh"
@@ -40,11 +41,24 @@ int cuda_fail(cudaError_t e, const char* what) {
     if (_e != cudaSuccess) return cuda_fail(_e, what); \
   } while (0)
 
-int set_device(int device) {
-  if (device < 0) return 0;
-  cudaError_t e = cudaSetDevice(device);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
-  return 0;
+// Makes `device` current for the rest of the calling entry point and restores the caller's
+// current device when it returns (device < 0: the current device).
+#define DUAL_USE_DEVICE(device)                                   \
+  dual::DeviceGuard device_guard_;                                \
+  do {                                                            \
+    cudaError_t _e = device_guard_.set(device);                   \
+    if (_e != cudaSuccess) return cuda_fail(_e, "cudaSetDevice"); \
+  } while (0)
+
+// `device`, or the calling thread's current device when it is negative.
+int resolve_device(int device) {
+  if (device >= 0) return device;
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return cur;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
@@ -67,7 +81,7 @@ size_t dual_decode_workspace_size(int batch, int num_ctas) {
   return dual::decode_workspace_bytes(batch, num_ctas);
 }
 
-int dual_decode_default_ctas(int device) { return dual::decode_default_grid_g(device < 0 ? 0 : device); }
+int dual_decode_default_ctas(int device) { return dual::decode_default_grid_g(resolve_device(device)); }
 
 int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_local,
                        const void* v_local, int64_t local_stride_bytes, int64_t local_capacity,
@@ -101,8 +115,8 @@ int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_h
         return fail(DUAL_EINVAL, "peer bank %d pointer null or not 16-byte aligned", i);
   }
   if (!(sm_scale > 0.0)) return fail(DUAL_EINVAL, "sm_scale must be positive");
-  if (int rc = set_device(device)) return rc;
-  if (num_ctas <= 0) num_ctas = dual::decode_default_grid_g(device < 0 ? 0 : device);
+  DUAL_USE_DEVICE(device);
+  if (num_ctas <= 0) num_ctas = dual::decode_default_grid_g(resolve_device(device));
   const size_t need = dual::decode_workspace_bytes(batch, num_ctas);
   if (workspace_bytes < need)
     return fail(DUAL_ENOSPACE, "workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
@@ -186,7 +200,7 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
         return fail(DUAL_EINVAL, "peer bank %d pointer null or not 16-byte aligned", i);
   }
   if (!(sm_scale > 0.0)) return fail(DUAL_EINVAL, "sm_scale must be positive");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   dual::AppendParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_stride_tok = q_stride_token;
@@ -244,7 +258,7 @@ int dual_stage_remote_rows(const void* const* peer_k, const void* const* peer_v,
     if (!peer_k[i] || !peer_v[i] || !stage_k[i] || !stage_v[i] || !aligned16(peer_k[i]) || !aligned16(peer_v[i]) ||
         !aligned16(stage_k[i]) || !aligned16(stage_v[i]))
       return fail(DUAL_EINVAL, "bank %d: bank or stage pointer null or not 16-byte aligned", i);
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   dual::StageParams p{};
   for (int i = 0; i < dual::kMaxPeers; ++i) {
     p.peer_k[i] = i < num_banks ? static_cast<const char*>(peer_k[i]) : nullptr;
@@ -287,7 +301,7 @@ int dual_stage_bank_range(const void* const* peer_k, const void* const* peer_v, 
       return fail(DUAL_EINVAL, "bank %d: row range [%lld, %lld) outside [0, %lld]", i, (long long)row_begin[i],
                   (long long)row_end[i], (long long)bank_slots);
   }
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   for (int i = 0; i < num_banks; ++i) {
     const int64_t rows = row_end[i] - row_begin[i];
     if (rows == 0) continue;
@@ -324,7 +338,7 @@ int dual_pack_read_order(int32_t* tier, int32_t* slot, int64_t table_rows, int64
                 tile_rows);
   if (history_out && !prefix_lens) return fail(DUAL_EINVAL, "history_out requires prefix_lens");
   if (local_capacity < 0 || local_capacity > 0x7ffffffeLL) return fail(DUAL_EINVAL, "local_capacity out of range");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   if (table_rows <= 0 || table_stride <= 0) return fail(DUAL_EINVAL, "empty page tables");
   dual::PackParams p{};
   p.tier = tier;
@@ -355,7 +369,7 @@ int dual_write_prefill_layout(int32_t* tier, int32_t* slot, int64_t table_rows, 
   if (batch < 0 || max_length < 0) return fail(DUAL_EINVAL, "negative batch or max_length");
   if (batch == 0 || max_length == 0) return DUAL_OK;
   if (!tier || !slot || !req_pool_indices || !prefix || !locations) return fail(DUAL_EINVAL, "null pointer argument");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   if (table_rows <= 0 || table_stride <= 0) return fail(DUAL_EINVAL, "empty page tables");
   dual::LayoutParams p{};
   p.tier = tier;
@@ -390,7 +404,7 @@ int dual_set_kv_buffer(void* k_local, void* v_local, int64_t local_stride_bytes,
       k_stride_token < row / 2 || v_stride_token < row / 2)
     return fail(DUAL_EINVAL, "k/v must be 16-byte aligned with token strides >= 1024 elements, multiples of 8");
   if (local_capacity < 0) return fail(DUAL_EINVAL, "local_capacity must be >= 0");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   dual::KvWriteParams p{};
   p.k_local = static_cast<char*>(k_local);
   p.v_local = static_cast<char*>(v_local);
@@ -421,7 +435,7 @@ int dual_migrate_copy(const int64_t* local_planes, const int64_t* remote_planes,
   if (num_planes <= 0 || num_banks <= 0) return fail(DUAL_EINVAL, "num_planes and num_banks must be positive");
   if (row_bytes <= 0 || (row_bytes & 15)) return fail(DUAL_EINVAL, "row_bytes must be a positive multiple of 16");
   if (local_slots <= 0 || remote_slots <= 0) return fail(DUAL_EINVAL, "pool sizes must be positive");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   dual::MigrateParams p{};
   p.local_planes = local_planes;
   p.remote_planes = remote_planes;
@@ -450,7 +464,7 @@ int dual_debug_inject(uint32_t mask) {
 int dual_status_clear(uint32_t* status, int device, void* stream) {
   g_last_error.clear();
   if (!status) return fail(DUAL_EINVAL, "null status");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   DUAL_CHECK_CUDA(cudaMemsetAsync(status, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream)), "status clear");
   return DUAL_OK;
 }
@@ -458,7 +472,7 @@ int dual_status_clear(uint32_t* status, int device, void* stream) {
 int dual_status_read(const uint32_t* status, uint32_t* value_out, int device, void* stream) {
   g_last_error.clear();
   if (!status || !value_out) return fail(DUAL_EINVAL, "null pointer argument");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DUAL_CHECK_CUDA(cudaMemcpyAsync(value_out, status, sizeof(uint32_t), cudaMemcpyDeviceToHost, s), "status read");
   DUAL_CHECK_CUDA(cudaStreamSynchronize(s), "status read sync");
@@ -469,7 +483,7 @@ int dual_status_read(const uint32_t* status, uint32_t* value_out, int device, vo
 int dual_supplier_alloc(int device, size_t bytes, void** ptr_out, unsigned char handle_out[64]) {
   g_last_error.clear();
   if (!ptr_out || !handle_out || bytes == 0) return fail(DUAL_EINVAL, "bad supplier_alloc arguments");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   void* ptr = nullptr;
   DUAL_CHECK_CUDA(cudaMalloc(&ptr, bytes), "cudaMalloc (supplier bank)");
   cudaIpcMemHandle_t h;
@@ -486,7 +500,7 @@ int dual_supplier_alloc(int device, size_t bytes, void** ptr_out, unsigned char 
 
 int dual_supplier_free(int device, void* ptr) {
   g_last_error.clear();
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   DUAL_CHECK_CUDA(cudaFree(ptr), "cudaFree (supplier bank)");
   return DUAL_OK;
 }
@@ -494,7 +508,7 @@ int dual_supplier_free(int device, void* ptr) {
 int dual_ipc_open(int device, const unsigned char handle[64], void** ptr_out) {
   g_last_error.clear();
   if (!handle || !ptr_out) return fail(DUAL_EINVAL, "null pointer argument");
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   cudaIpcMemHandle_t h;
   std::memcpy(&h, handle, 64);
   DUAL_CHECK_CUDA(cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
@@ -503,7 +517,7 @@ int dual_ipc_open(int device, const unsigned char handle[64], void** ptr_out) {
 
 int dual_ipc_close(int device, void* ptr) {
   g_last_error.clear();
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   DUAL_CHECK_CUDA(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
   return DUAL_OK;
 }
@@ -520,7 +534,7 @@ int dual_enable_peer(int device, int peer) {
   int can = 0;
   DUAL_CHECK_CUDA(cudaDeviceCanAccessPeer(&can, device, peer), "cudaDeviceCanAccessPeer");
   if (!can) return fail(DUAL_EUNSUPPORTED, "device %d cannot access peer %d", device, peer);
-  if (int rc = set_device(device)) return rc;
+  DUAL_USE_DEVICE(device);
   cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
   if (e == cudaErrorPeerAccessAlreadyEnabled) {
     cudaGetLastError();

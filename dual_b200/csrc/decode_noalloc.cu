@@ -19,7 +19,11 @@
 //     (cudaGetSymbolAddress with that device current) and caches it; make that
 //     first call before any stream capture on the device;
 //   * sizes beyond the array are rejected: (num_ctas + batch) segments of
-//     32 q heads x 132 floats, plus a 256-byte header, must fit in 8 MiB.
+//     32 q heads x 132 floats, plus a 256-byte header, must fit in 8 MiB;
+//   * with status == NULL the kernels record their status bits (bad page ids,
+//     timed-out waits) in the array's own header word, which each such call
+//     clears first; dual_decode_noalloc_status reads it back, and it is only
+//     meaningful until the next call on the device.
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -27,6 +31,7 @@
 
 #include "dual_b200.h"
 #include "decode.cuh"
+#include "device_guard.h"
 
 namespace dual {
 void set_last_error_message(const char* message);  // capi.cu
@@ -53,13 +58,26 @@ int noalloc_fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// `device`, or the calling thread's current device when it is negative (as for dual_tiered_decode).
+int resolve_device(int device, int* out) {
+  if (device < 0) {
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  }
+  if (device >= kMaxDevices) return noalloc_fail(DUAL_EINVAL, "device index %d out of range", device);
+  *out = device;
+  return DUAL_OK;
+}
+
 // Device address of g_decode_scratch on `device` (looked up once per device,
-// with that device current).  In host code the symbol itself is only a host
-// stand-in and must never be handed to a kernel.
+// with that device current; the caller's current device is restored).  In host
+// code the symbol itself is only a host stand-in and must never be handed to a
+// kernel.
 int scratch_address(int device, void** out) {
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_scratch_ptr[device] == nullptr) {
-    cudaError_t e = cudaSetDevice(device);
+    dual::DeviceGuard guard;
+    cudaError_t e = guard.set(device);
     if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
@@ -84,7 +102,6 @@ extern "C" int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token,
                                           int64_t out_stride_head, float* lse, uint32_t* status, int num_ctas,
                                           int device, void* stream) {
   dual::set_last_error_message("");
-  if (device < 0 || device >= kMaxDevices) return noalloc_fail(DUAL_EINVAL, "device index %d out of range", device);
   if (batch < 0) return noalloc_fail(DUAL_EINVAL, "batch must be >= 0 (got %d)", batch);
   if (batch == 0) return DUAL_OK;
   if (!q || !k_local || !v_local || !kv_indptr || !unified_indices || !out)
@@ -108,6 +125,7 @@ extern "C" int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token,
         return noalloc_fail(DUAL_EINVAL, "peer bank %d pointer null or not 16-byte aligned", i);
   }
   if (!(sm_scale > 0.0)) return noalloc_fail(DUAL_EINVAL, "sm_scale must be positive");
+  if (int rc = resolve_device(device, &device)) return rc;
   if (num_ctas <= 0) num_ctas = dual::decode_default_grid_g(device);
   const size_t need = dual::decode_workspace_bytes(batch, num_ctas);
   if (need > kNoAllocScratchBytes)
@@ -118,7 +136,8 @@ extern "C" int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token,
                         (kNoAllocScratchBytes - 256) / (sizeof(float) * dual::DecodeCfg::ROWS * dual::kPartialStride));
   void* scratch = nullptr;
   if (int rc = scratch_address(device, &scratch)) return rc;
-  cudaError_t e = cudaSetDevice(device);
+  dual::DeviceGuard guard;
+  cudaError_t e = guard.set(device);
   if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned* status_word = reinterpret_cast<unsigned*>(status);
@@ -158,5 +177,21 @@ extern "C" int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token,
   p.lse = lse;
   e = dual::launch_tiered_decode(p, s);
   if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "tiered decode launch: %s", cudaGetErrorString(e));
+  return DUAL_OK;
+}
+
+extern "C" int dual_decode_noalloc_status(uint32_t* value_out, int device, void* stream) {
+  dual::set_last_error_message("");
+  if (value_out == nullptr) return noalloc_fail(DUAL_EINVAL, "null value_out");
+  if (int rc = resolve_device(device, &device)) return rc;
+  void* scratch = nullptr;
+  if (int rc = scratch_address(device, &scratch)) return rc;
+  dual::DeviceGuard guard;
+  cudaError_t e = guard.set(device);
+  if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  e = cudaMemcpyAsync(value_out, scratch, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "status read: %s", cudaGetErrorString(e));
   return DUAL_OK;
 }

@@ -90,9 +90,10 @@ int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_h
  * All calls on a device share that array and it keeps the last call's contents: calls
  * that overlap on the GPU race on it.  The first call on a device looks up the array's
  * address (with that device current); make it before any stream capture.
- * status: NULL (this call clears the array's own status word and records into it) or a
- * caller-owned device status word that kernels OR bits into.  Other arguments as for
- * dual_tiered_decode. */
+ * status: NULL (this call clears the array's own status word and records into it; read it
+ * back with dual_decode_noalloc_status before the next call on the device) or a caller-owned
+ * device status word that kernels OR bits into.  Other arguments as for dual_tiered_decode,
+ * device < 0 included (the calling thread's current device). */
 int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                                const void* k_local, const void* v_local, int64_t local_stride_bytes,
                                int64_t local_capacity,
@@ -102,6 +103,11 @@ int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_
                                int64_t num_indices, int batch, double sm_scale,
                                void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
                                uint32_t* status, int num_ctas, int device, void* stream);
+/* Part of the allocation-free decode above (no reference counterpart): copies the status word of
+ * the device's scratch array -- the bits of the last dual_tiered_decode_noalloc call on `device`
+ * that was given status == NULL -- to *value_out once the work queued on `stream` has finished.
+ * Synchronous (not capturable); allocates nothing. */
+int dual_decode_noalloc_status(uint32_t* value_out, int device, void* stream);
 
 /* ------------------------------------------------------ tiered append ---
  * Replaces the tiered FA2 batch-prefill module on the append path (run hook
