@@ -73,7 +73,7 @@ void set_last_error_message(const char* message) { g_last_error = message ? mess
 extern "C" {
 
 const char* dual_last_error(void) { return g_last_error.c_str(); }
-int dual_abi_version(void) { return 100; }
+int dual_abi_version(void) { return 200; }
 
 size_t dual_decode_workspace_size(int batch, int num_ctas) {
   if (batch < 0) batch = 0;
@@ -143,7 +143,8 @@ int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.batch = batch;
   p.scale_log2 = static_cast<float>(sm_scale * 1.4426950408889634);
   p.status = static_cast<unsigned*>(workspace);
-  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+  p.counters = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + 256);
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + dual::decode_workspace_head_bytes(batch));
   p.grid_g = num_ctas;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride_tok = out_stride_token;
@@ -151,6 +152,17 @@ int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.lse = lse;
   cudaError_t e = dual::launch_tiered_decode(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tiered decode launch");
+  return DUAL_OK;
+}
+
+int dual_decode_workspace_reset(void* workspace, size_t workspace_bytes, int batch, int device, void* stream) {
+  g_last_error.clear();
+  if (!workspace || batch < 0) return fail(DUAL_EINVAL, "null workspace or negative batch");
+  const size_t head = dual::decode_workspace_head_bytes(batch);
+  if (workspace_bytes < head) return fail(DUAL_ENOSPACE, "workspace too small: need %zu bytes, got %zu", head,
+                                          workspace_bytes);
+  DUAL_USE_DEVICE(device);
+  DUAL_CHECK_CUDA(cudaMemsetAsync(workspace, 0, head, static_cast<cudaStream_t>(stream)), "workspace reset");
   return DUAL_OK;
 }
 
@@ -169,14 +181,22 @@ int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_hos
   return DUAL_OK;
 }
 
+int dual_append_share_flags(const int32_t* kv_indptr_host, int batch, int64_t* count) {
+  g_last_error.clear();
+  if (batch < 0 || !count || (batch > 0 && !kv_indptr_host)) return fail(DUAL_EINVAL, "bad share flag arguments");
+  *count = dual::append_share_flags(kv_indptr_host, batch);
+  return DUAL_OK;
+}
+
 int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_local,
                        const void* v_local, int64_t local_stride_bytes, int64_t local_capacity,
                        const void* const* peer_k, const void* const* peer_v, int num_peers,
                        int64_t peer_stride_bytes, int64_t peer_slots, const int32_t* qo_indptr,
                        const int32_t* kv_indptr, const int32_t* unified_indices, int64_t num_indices, int batch,
                        int causal, double sm_scale, const int32_t* work, int64_t num_work, void* out,
-                       int64_t out_stride_token, int64_t out_stride_head, float* lse, uint32_t* status, int device,
-                       void* stream) {
+                       int64_t out_stride_token, int64_t out_stride_head, float* lse, uint32_t* status,
+                       void* const* stage_k, void* const* stage_v, int64_t stage_stride_bytes,
+                       uint32_t* share_flags, int64_t num_share_flags, int device, void* stream) {
   g_last_error.clear();
   if (batch < 0 || num_work < 0) return fail(DUAL_EINVAL, "negative batch or work count");
   if (batch == 0 || num_work == 0) return DUAL_OK;
@@ -200,6 +220,15 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
         return fail(DUAL_EINVAL, "peer bank %d pointer null or not 16-byte aligned", i);
   }
   if (!(sm_scale > 0.0)) return fail(DUAL_EINVAL, "sm_scale must be positive");
+  if (share_flags != nullptr) {
+    if (num_peers == 0 || !stage_k || !stage_v || num_share_flags <= 0)
+      return fail(DUAL_EINVAL, "remote-row sharing needs suppliers, one stage buffer pair per bank and flags");
+    if ((stage_stride_bytes & 15) || stage_stride_bytes < min_stride)
+      return fail(DUAL_EINVAL, "stage buffers need a 16-byte multiple slot stride >= 2048 B");
+    for (int i = 0; i < num_peers; ++i)
+      if (!stage_k[i] || !stage_v[i] || !aligned16(stage_k[i]) || !aligned16(stage_v[i]))
+        return fail(DUAL_EINVAL, "stage buffer %d pointer null or not 16-byte aligned", i);
+  }
   DUAL_USE_DEVICE(device);
   dual::AppendParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -231,6 +260,19 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.lse = lse;
   p.status = status;
   p.inject = g_inject.load(std::memory_order_relaxed);
+  if (share_flags != nullptr) {
+    for (int i = 0; i < dual::kMaxPeers; ++i) {
+      p.stage_k[i] = i < num_peers ? static_cast<const char*>(stage_k[i]) : nullptr;
+      p.stage_v[i] = i < num_peers ? static_cast<const char*>(stage_v[i]) : nullptr;
+    }
+    p.stage_stride = stage_stride_bytes;
+    p.share_flags = share_flags;
+    p.num_share_flags = num_share_flags;
+    // every chunk starts unclaimed in every launch
+    DUAL_CHECK_CUDA(cudaMemsetAsync(share_flags, 0, size_t(num_share_flags) * sizeof(uint32_t),
+                                    static_cast<cudaStream_t>(stream)),
+                    "share flag clear");
+  }
   cudaError_t e = dual::launch_tiered_append(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tiered append launch");
   return DUAL_OK;

@@ -48,6 +48,55 @@ __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
 
 constexpr float kDecodeRescale = 8.0f;  // log2 units
 
+// Split of the flattened token axis [0, T) over G CTAs: CTA g owns [g T / G, (g + 1) T / G).
+struct Split {
+  int64_t T;
+  int G;
+  __device__ __forceinline__ int owner(int64_t x) const { return int(((x + 1) * G - 1) / T); }
+  __device__ __forceinline__ bool nonempty(int g) const { return (int64_t(g) * T) / G < (int64_t(g + 1) * T) / G; }
+  // [start, end) of request b, clamped into [0, T]
+  __device__ __forceinline__ void range(const int32_t* indptr, int b, int64_t& start, int64_t& end) const {
+    start = __ldg(indptr + b);
+    end = __ldg(indptr + b + 1);
+    start = start < 0 ? 0 : (start > T ? T : start);
+    end = end < start ? start : (end > T ? T : end);
+  }
+};
+
+// Combine the partial states of request b for the 4 q heads of kv head h (one warp) and write the
+// bf16 output and the base-2 LSE.  CTAs glo..ghi cover the request; those with an empty range
+// wrote nothing.  Partials are read through L2 (other SMs wrote them during this launch).
+__device__ __noinline__ void merge_request_heads(const TieredDecodeParams& p, const Split& sp, int b, int h,
+                                                    int glo, int ghi, int lane) {
+  constexpr int64_t kSeg = int64_t(kNumQoHeads) * kPartialStride;
+  for (int r = 0; r < kGqa; ++r) {
+    const int row = h * kGqa + r;
+    const float* base = p.partial + (int64_t(b) * kNumQoHeads + row) * kPartialStride;
+    float M = -INFINITY;
+    for (int gg = glo; gg <= ghi; ++gg)
+      if (sp.nonempty(gg)) M = fmaxf(M, __ldcg(base + gg * kSeg + kHeadDim));
+    float D = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int gg = glo; gg <= ghi; ++gg) {
+      if (!sp.nonempty(gg)) continue;
+      const float* src = base + gg * kSeg;
+      const float mm = __ldcg(src + kHeadDim);
+      const float w = (mm == -INFINITY) ? 0.f : exp2f(mm - M);
+      D += w * __ldcg(src + kHeadDim + 1);
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+    const float inv = 1.f / D;
+    __nv_bfloat16* orow = p.out + int64_t(b) * p.out_stride_tok + int64_t(row) * p.out_stride_head;
+    reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[0] = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+    reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[1] = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    if (p.lse != nullptr && lane == 0) p.lse[int64_t(b) * kNumQoHeads + row] = M + log2f(D);
+  }
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __grid_constant__ TieredDecodeParams p) {
   constexpr int NS = Cfg::NS, TILE = Cfg::TILE, CONS = Cfg::CONSUMERS;
@@ -88,6 +137,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __
   }
   const int64_t lo = (int64_t(g) * T) / G;
   const int64_t hi = (int64_t(g + 1) * T) / G;
+  const Split sp{T, G};
 
   if (warp == CONS) {
     // ------------------------------------------------------------ producer
@@ -283,68 +333,71 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar + stage);
     if (it.last_in_segment()) {
-      // ---- flush this request segment as one partial state (unnormalised O, m, d)
       float d_row = d_run;
       d_row += __shfl_xor_sync(0xffffffffu, d_row, 1);
       d_row += __shfl_xor_sync(0xffffffffu, d_row, 2);
+      int64_t start, end;
+      sp.range(p.indptr, cur_b, start, end);
+      const bool whole = start >= lo && end <= hi;  // the request lies inside this CTA's range
       if (gi < kGqa) {
-        float* dst = p.partial + (int64_t(g + cur_b) * Cfg::ROWS + h * kGqa + gi) * kPartialStride;
+        if (whole) {
+          // ---- normalise and write the output directly
+          const float inv = 1.f / d_row;
+          __nv_bfloat16* orow =
+              p.out + int64_t(cur_b) * p.out_stride_tok + int64_t(h * kGqa + gi) * p.out_stride_head;
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt)
-          *reinterpret_cast<float2*>(dst + nt * 8 + 2 * ci) = make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
-        if (ci == 0) *reinterpret_cast<float2*>(dst + kHeadDim) = make_float2(m_run, d_row);
+          for (int nt = 0; nt < 16; ++nt)
+            *reinterpret_cast<__nv_bfloat162*>(orow + nt * 8 + 2 * ci) =
+                __floats2bfloat162_rn((o[nt][0] + o[nt][2]) * inv, (o[nt][1] + o[nt][3]) * inv);
+          if (ci == 0 && p.lse != nullptr) p.lse[int64_t(cur_b) * kNumQoHeads + h * kGqa + gi] = m_run + log2f(d_row);
+        } else {
+          // ---- one partial state (unnormalised O, m, d) of a request split across CTAs
+          float* dst = p.partial + (int64_t(g + cur_b) * Cfg::ROWS + h * kGqa + gi) * kPartialStride;
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt)
+            *reinterpret_cast<float2*>(dst + nt * 8 + 2 * ci) = make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
+          if (ci == 0) *reinterpret_cast<float2*>(dst + kHeadDim) = make_float2(m_run, d_row);
+        }
       }
       reset_state();
+      if (!whole) {
+        // the last of the request's CTAs to arrive for this kv head merges the partial states
+        __syncwarp();
+        const int glo = sp.owner(start), ghi = sp.owner(end - 1);
+        int segments = 0;
+        for (int gg = glo; gg <= ghi; ++gg) segments += sp.nonempty(gg) ? 1 : 0;
+        unsigned last = 0;
+        if (lane == 0) {
+          __threadfence();  // this warp's partial is visible before its arrival is counted
+          unsigned* cnt = p.counters + int64_t(cur_b) * kNumKvHeads + h;
+          last = atomicAdd(cnt, 1u) == unsigned(segments - 1) ? 1u : 0u;
+          if (last) *cnt = 0u;  // every arrival of this launch is in: ready for the next launch
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          merge_request_heads(p, sp, cur_b, h, glo, ghi, lane);
+        }
+      }
     }
   }
-}
 
-// Combine the partial states of each (request, q head) and write the output.
-constexpr int kMergeRows = 8;  // q heads per merge block (one warp each)
-
-__global__ void __launch_bounds__(kMergeRows * 32) decode_merge_kernel(const __grid_constant__ TieredDecodeParams p) {
-  const int b = blockIdx.x;
-  const int row = blockIdx.y * kMergeRows + (threadIdx.x >> 5);  // q head
-  const int lane = threadIdx.x & 31;
-  const int G = p.grid_g;
-  int64_t T = __ldg(p.indptr + p.batch);
-  if (T > p.num_indices || T < 0) T = T < 0 ? 0 : p.num_indices;
-  int64_t start = __ldg(p.indptr + b), end = __ldg(p.indptr + b + 1);
-  start = start < 0 ? 0 : (start > T ? T : start);
-  end = end < start ? start : (end > T ? T : end);
-  __nv_bfloat16* orow = p.out + int64_t(b) * p.out_stride_tok + int64_t(row) * p.out_stride_head;
-  if (end <= start || T <= 0) {
-    for (int d = lane; d < kHeadDim; d += 32) orow[d] = __float2bfloat16(0.f);
-    if (p.lse != nullptr && lane == 0) p.lse[int64_t(b) * kNumQoHeads + row] = -INFINITY;
-    return;
+  // ---- requests with no KV entries: output 0, LSE -inf, written by the CTA that owns their
+  // position in the token axis (the last CTA for positions at the end; CTA 0 when T = 0)
+  for (int b = lane; b < p.batch; b += 32) {
+    int64_t start, end;
+    sp.range(p.indptr, b, start, end);
+    if (end > start) continue;
+    const int own = T == 0 ? 0 : (start < T ? sp.owner(start) : G - 1);
+    if (own != g) continue;
+    for (int r = 0; r < kGqa; ++r) {
+      const int row = h * kGqa + r;
+      __nv_bfloat16* orow = p.out + int64_t(b) * p.out_stride_tok + int64_t(row) * p.out_stride_head;
+      for (int d = 0; d < kHeadDim; d += 2)
+        *reinterpret_cast<__nv_bfloat162*>(orow + d) = __floats2bfloat162_rn(0.f, 0.f);
+      if (p.lse != nullptr) p.lse[int64_t(b) * kNumQoHeads + row] = -INFINITY;
+    }
   }
-  auto gof = [&](int64_t x) -> int { return int(((x + 1) * G - 1) / T); };
-  // CTAs with an empty range (T < G) wrote no partial state: skip them.
-  auto nonempty = [&](int gg) { return (int64_t(gg) * T) / G < (int64_t(gg + 1) * T) / G; };
-  const int glo = gof(start), ghi = gof(end - 1);
-  constexpr int64_t kSeg = int64_t(DecodeCfg::ROWS) * kPartialStride;
-  const float* base = p.partial + (int64_t(b) * DecodeCfg::ROWS + row) * kPartialStride;
-  float M = -INFINITY;
-  for (int gg = glo; gg <= ghi; ++gg)
-    if (nonempty(gg)) M = fmaxf(M, base[gg * kSeg + kHeadDim]);
-  float D = 0.f;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int gg = glo; gg <= ghi; ++gg) {
-    if (!nonempty(gg)) continue;
-    const float* src = base + gg * kSeg;
-    const float mm = src[kHeadDim];
-    const float w = (mm == -INFINITY) ? 0.f : exp2f(mm - M);
-    D += w * src[kHeadDim + 1];
-    const float4 v = *reinterpret_cast<const float4*>(src + lane * 4);
-    acc[0] += w * v.x;
-    acc[1] += w * v.y;
-    acc[2] += w * v.z;
-    acc[3] += w * v.w;
-  }
-  const float inv = 1.f / D;
-  reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[0] = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
-  reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[1] = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
-  if (p.lse != nullptr && lane == 0) p.lse[int64_t(b) * kNumQoHeads + row] = M + log2f(D);
 }
 
 }  // namespace
@@ -361,13 +414,7 @@ cudaError_t launch_tiered_decode(const TieredDecodeParams& p, cudaStream_t strea
   if (cudaError_t e = set_max_dynamic_smem_once(tiered_decode_kernel<Cfg>, Cfg::SMEM_BYTES, configured))
     return e;
   tiered_decode_kernel<Cfg><<<p.grid_g, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  if (p.batch > 0) {
-    decode_merge_kernel<<<dim3(p.batch, kNumQoHeads / kMergeRows), kMergeRows * 32, 0, stream>>>(p);
-    e = cudaGetLastError();
-  }
-  return e;
+  return cudaGetLastError();
 }
 
 }  // namespace dual

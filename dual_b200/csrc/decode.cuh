@@ -20,9 +20,13 @@
 //   * 8 consumer warps, one per kv head, compute every tile with bf16
 //     m16n8k16 tensor-core MMAs (the 4 query heads of the GQA group are the
 //     MMA rows) and an exp2-domain online softmax.
-//   * Partial (O, m, d) states go to the workspace; a merge kernel combines
-//     them per (request, q head) with a log-sum-exp reduction and writes the
-//     bf16 output and the base-2 LSE (FlashInfer's convention).
+//   * A request that lies inside one CTA's range is normalised in registers
+//     and written directly.  A request split across CTAs leaves one partial
+//     (O, m, d) state per CTA in the workspace; the last warp to finish a
+//     (request, kv head) -- found with a per-(request, kv head) arrival
+//     counter -- combines them with a log-sum-exp reduction and writes the
+//     bf16 output and the base-2 LSE (FlashInfer's convention), then resets
+//     the counter for the next launch.  No second kernel.
 #pragma once
 #include "common.cuh"
 
@@ -52,7 +56,8 @@ struct TieredDecodeParams {
   int64_t num_indices;     // capacity of `indices` (reads never go beyond it)
   int batch;
   float scale_log2;        // sm_scale * log2(e)
-  float* partial;          // workspace
+  float* partial;          // workspace: partial states
+  unsigned* counters;      // workspace: arrival counter per (request, kv head), zero between launches
   unsigned* status;        // workspace status word
   int grid_g;              // CTAs per head group
   __nv_bfloat16* out;      // [B, 32, 128]
@@ -83,9 +88,14 @@ struct DecodeConfig {
 
 using DecodeCfg = DecodeConfig<3, 16>;
 
-// Workspace layout: [status: 256 B][partials: (G + B) segments x 32 q heads x 132 floats].
+// Workspace layout: [status: 256 B][counters: batch x 8 kv heads x 4 B, rounded up to 256 B]
+//                   [partials: (G + B) segments x 32 q heads x 132 floats].
+inline size_t decode_counter_bytes(int batch) {
+  return (size_t(batch) * kNumKvHeads * sizeof(unsigned) + 255) / 256 * 256;
+}
+inline size_t decode_workspace_head_bytes(int batch) { return 256 + decode_counter_bytes(batch); }
 inline size_t decode_workspace_bytes(int batch, int grid_g) {
-  return 256 + sizeof(float) * size_t(grid_g + batch) * DecodeCfg::ROWS * kPartialStride;
+  return decode_workspace_head_bytes(batch) + sizeof(float) * size_t(grid_g + batch) * DecodeCfg::ROWS * kPartialStride;
 }
 
 cudaError_t launch_tiered_decode(const TieredDecodeParams& p, cudaStream_t stream);

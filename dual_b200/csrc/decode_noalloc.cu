@@ -19,7 +19,10 @@
 //     (cudaGetSymbolAddress with that device current) and caches it; make that
 //     first call before any stream capture on the device;
 //   * sizes beyond the array are rejected: (num_ctas + batch) segments of
-//     32 q heads x 132 floats, plus a 256-byte header, must fit in 8 MiB;
+//     32 q heads x 132 floats, plus a 256-byte header and batch x 8 arrival
+//     counters (rounded up to 256 bytes), must fit in 8 MiB;
+//   * every call clears the arrival counters before its kernel, so a call
+//     never depends on what an earlier one left in the array;
 //   * with status == NULL the kernels record their status bits (bad page ids,
 //     timed-out waits) in the array's own header word, which each such call
 //     clears first; dual_decode_noalloc_status reads it back, and it is only
@@ -42,7 +45,7 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 constexpr int kMaxDevices = 64;
 
-// Scratch of the allocation-free decode: [status word: 256 B][partials].
+// Scratch of the allocation-free decode: [status word: 256 B][arrival counters][partials].
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
 
 std::mutex g_mu;
@@ -133,7 +136,8 @@ extern "C" int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token,
                         "batch %d with %d CTAs needs %zu bytes of scratch; the allocation-free entry point holds "
                         "%zu (num_ctas + batch <= %zu)",
                         batch, num_ctas, need, kNoAllocScratchBytes,
-                        (kNoAllocScratchBytes - 256) / (sizeof(float) * dual::DecodeCfg::ROWS * dual::kPartialStride));
+                        (kNoAllocScratchBytes - dual::decode_workspace_head_bytes(batch)) /
+                            (sizeof(float) * dual::DecodeCfg::ROWS * dual::kPartialStride));
   void* scratch = nullptr;
   if (int rc = scratch_address(device, &scratch)) return rc;
   dual::DeviceGuard guard;
@@ -147,6 +151,11 @@ extern "C" int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token,
     e = cudaMemsetAsync(status_word, 0, sizeof(unsigned), s);
     if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "status clear: %s", cudaGetErrorString(e));
   }
+  // Arrival counters start at zero in every call (an earlier call that gave up on a wait may have
+  // left some behind).
+  unsigned* counters = reinterpret_cast<unsigned*>(static_cast<char*>(scratch) + 256);
+  e = cudaMemsetAsync(counters, 0, dual::decode_counter_bytes(batch), s);
+  if (e != cudaSuccess) return noalloc_fail(DUAL_ECUDA, "counter clear: %s", cudaGetErrorString(e));
 
   dual::TieredDecodeParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -169,7 +178,8 @@ extern "C" int dual_tiered_decode_noalloc(const void* q, int64_t q_stride_token,
   p.batch = batch;
   p.scale_log2 = static_cast<float>(sm_scale * 1.4426950408889634);
   p.status = status_word;
-  p.partial = reinterpret_cast<float*>(static_cast<char*>(scratch) + 256);
+  p.counters = counters;
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(scratch) + dual::decode_workspace_head_bytes(batch));
   p.grid_g = num_ctas;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride_tok = out_stride_token;

@@ -60,7 +60,10 @@ __device__ __forceinline__ bool resolve_row(const MigrateParams& p, int64_t w, c
 
 constexpr int kCopyThreads = 256;
 
-__global__ void __launch_bounds__(kCopyThreads) migrate_copy_kernel(const __grid_constant__ MigrateParams p) {
+// At most 64 registers a thread (16,384 per CTA), so one copy CTA fits on an SM beside a running
+// decode CTA (288 threads x 168 registers = 48,384 of the SM's 65,536): a migration launched while
+// decode holds every SM then runs alongside it instead of only in the gaps between layers.
+__global__ void __launch_bounds__(kCopyThreads, 4) migrate_copy_kernel(const __grid_constant__ MigrateParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = int64_t(gridDim.x) * (kCopyThreads / 32);
   const int64_t warp_id = int64_t(blockIdx.x) * (kCopyThreads / 32) + (threadIdx.x >> 5);

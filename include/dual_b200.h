@@ -39,7 +39,9 @@ extern "C" {
 
 /* Thread-local message of the last failing call ("" if none). */
 const char* dual_last_error(void);
-/* ABI version of this library (major * 100 + minor). */
+/* ABI version of this library (major * 100 + minor): 200 = the merge inside the decode kernel (a
+ * workspace with arrival counters, dual_decode_workspace_reset) and remote-row sharing arguments on
+ * dual_tiered_append. */
 int dual_abi_version(void);
 
 /* ------------------------------------------------------- tiered decode ---
@@ -63,11 +65,22 @@ int dual_abi_version(void);
  * out         [batch, 32, 128] bf16; lse [batch, 32] fp32 (base 2, FlashInfer's
  *             convention) or NULL
  * workspace   device scratch of >= dual_decode_workspace_size(batch, num_ctas)
- *             bytes; its first 4 bytes are the status word (cleared by
- *             dual_status_clear, never by this call)
+ *             bytes, 256-byte aligned: [status word, 256 B][one arrival counter per
+ *             (request, kv head)][partial softmax states].  Zero its head once with
+ *             dual_decode_workspace_reset before the first call (or allocate it
+ *             zeroed); launches leave the counters at zero again, so one reset per
+ *             workspace is enough -- except after a launch whose status word shows
+ *             DUAL_STATUS_WAIT_TIMEOUT or DUAL_STATUS_BAD_LENGTH, which may leave
+ *             counters behind.  The status word is cleared by dual_status_clear or
+ *             the reset, never by this call.
  * num_ctas    CTAs (0 = one per SM); fixed per graph capture
+ * A request split over several CTAs is merged by the last of them to finish, inside the same
+ * kernel (one launch per call).
  */
 size_t dual_decode_workspace_size(int batch, int num_ctas);
+/* Zeroes the status word and the arrival counters of a decode workspace for up to `batch` requests
+ * (asynchronous on `stream`, capturable). */
+int dual_decode_workspace_reset(void* workspace, size_t workspace_bytes, int batch, int device, void* stream);
 int dual_decode_default_ctas(int device);
 int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                        const void* k_local, const void* v_local, int64_t local_stride_bytes,
@@ -85,8 +98,9 @@ int dual_tiered_decode(const void* q, int64_t q_stride_token, int64_t q_stride_h
  * process whose memory manager already owns almost all of HBM and forbids out-of-band
  * cudaMalloc, or a foreign-language binding that only holds the attention tensors).
  * The split-KV partial states live in a fixed 8 MiB file-scope device array that every
- * GPU loading this library holds until exit; (num_ctas + batch) * 16896 + 256 bytes must
- * fit in it (e.g. batch <= 348 with the default 148 CTAs), otherwise DUAL_ENOSPACE.
+ * GPU loading this library holds until exit; (num_ctas + batch) * 16896 + 256 bytes plus
+ * batch * 32 bytes of arrival counters (rounded up to 256) must fit in it (e.g. batch <= 347
+ * with the default 148 CTAs), otherwise DUAL_ENOSPACE.  Each call zeroes the counters first.
  * All calls on a device share that array and it keeps the last call's contents: calls
  * that overlap on the GPU race on it.  The first call on a device looks up the array's
  * address (with that device current); make it before any stream capture.
@@ -119,14 +133,24 @@ int dual_decode_noalloc_status(uint32_t* value_out, int device, void* stream);
  * causal != 0 query token i sees entry j iff j < L_b - q_b (history, any order) or
  * j - (L_b - q_b) <= i (the query suffix, in order -- the packer's Full list).
  * dual_append_plan (host): from HOST copies of qo_indptr / kv_indptr, writes the work list
- * (4 int32 per item: request, kv head, 64-token query pair, 128-entry kv tiles), grouped by
- * (request, kv head) so a group's items run together and share K/V rows in L2, groups longest
- * first and pairs longest first within a group; returns the item count in *num_work (call with
- * work=NULL to size it).  The work list is then copied to
+ * (4 int32 per item: request, kv head, 64-token query pair, index of the request's first 64-entry
+ * list chunk), grouped by (request, kv head) so a group's items run together and share K/V rows in
+ * L2, groups longest first and pairs longest first within a group; returns the item count in
+ * *num_work (call with work=NULL to size it).  The work list is then copied to
  * the device and passed to dual_tiered_append with the DEVICE indptrs.
- * q/out [sum q, 32, 128] bf16; lse [sum q, 32] fp32 base 2 or NULL; status: device word. */
+ * q/out [sum q, 32, 128] bf16; lse [sum q, 32] fp32 base 2 or NULL; status: device word.
+ * Remote-row sharing (optional; share_flags = NULL reads supplier rows in place per item): a
+ * supplier row crosses NVLink once per work item that reads it, i.e. once per 64-token query pair
+ * of its request (a peer's memory is not cached in the local L2).  With share_flags, the items of a
+ * (request, kv head) fetch each 64-entry list chunk that holds remote rows once: the group's longest
+ * query pair reads it from the suppliers and writes its remote rows into stage_k / stage_v[b] (local
+ * buffers laid out like bank b, stage_stride_bytes per row, as many rows as peer_slots); the others
+ * wait (bounded; afterwards they read the suppliers) and read them from there.  share_flags holds
+ * num_share_flags = dual_append_share_flags(...) 32-bit words, zeroed by this call before the
+ * kernel; results do not depend on the sharing. */
 int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, int batch, int causal,
                      int32_t* work_host, int64_t max_work, int64_t* num_work);
+int dual_append_share_flags(const int32_t* kv_indptr_host, int batch, int64_t* count);
 int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                        const void* k_local, const void* v_local, int64_t local_stride_bytes,
                        int64_t local_capacity,
@@ -136,7 +160,8 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
                        const int32_t* unified_indices, int64_t num_indices, int batch, int causal,
                        double sm_scale, const int32_t* work, int64_t num_work,
                        void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
-                       uint32_t* status, int device, void* stream);
+                       uint32_t* status, void* const* stage_k, void* const* stage_v, int64_t stage_stride_bytes,
+                       uint32_t* share_flags, int64_t num_share_flags, int device, void* stream);
 
 /* ------------------------------------------------------ read-order packer ---
  * Replaces Triton _count_remote/_pack_indices + Engine.prepare (peer/backend.py:22-79)

@@ -24,7 +24,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} missing from the ctypes signature table"
     assert set(_lib.SIGNATURES) == set(names)
-    assert lib.dual_abi_version() == 100
+    assert lib.dual_abi_version() == 200
 
 
 def test_argument_errors_are_codes_not_crashes():
@@ -83,9 +83,17 @@ def test_fault_injection_mask_is_validated():
 
 def test_workspace_size_formula():
     lib = _lib.load()
-    # 256 B header + (G + B) segments x 32 q heads x 132 floats
-    assert lib.dual_decode_workspace_size(64, 148) == 256 + (148 + 64) * 32 * 132 * 4
-    assert lib.dual_decode_workspace_size(1, 1) == 256 + 2 * 32 * 132 * 4
+    # 256 B header + B x 8 arrival counters (rounded up to 256 B) + (G + B) segments x 32 q heads x 132 floats
+    assert lib.dual_decode_workspace_size(64, 148) == 256 + 2048 + (148 + 64) * 32 * 132 * 4
+    assert lib.dual_decode_workspace_size(1, 1) == 256 + 256 + 2 * 32 * 132 * 4
+    assert lib.dual_decode_workspace_size(9, 4) == 256 + 512 + 13 * 32 * 132 * 4
+
+
+def test_workspace_reset_checks_size_before_any_launch():
+    lib = _lib.load()
+    assert lib.dual_decode_workspace_reset(None, 4096, 4, -1, None) == 1
+    assert lib.dual_decode_workspace_reset(256, 300, 64, -1, None) == 3
+    assert b"too small" in lib.dual_last_error()
 
 
 def test_no_cpu_fallback(monkeypatch, tmp_path):

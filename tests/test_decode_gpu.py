@@ -257,3 +257,36 @@ def test_decode_strided_views_and_other_scale():
     torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
     assert bool((wide[:, :4] == 3.0).all()) and bool((wide[:, 36:] == 3.0).all())  # nothing outside the view
     assert _status(ws) == 0
+
+
+def test_one_workspace_many_launches_counters_return_to_zero():
+    """Requests split across CTAs are merged inside the decode kernel: the last CTA to finish a
+    (request, kv head) merges, found through an arrival counter in the workspace that it resets.  One
+    workspace, zeroed once, then serves launches of different batches and CTA counts (which change
+    which requests are split, whole or empty), and every counter is back at zero after each."""
+    runs = []
+    for case in (C.config1(banks=3), C.validate_case(4), C.validate_case(3, banks=3)):
+        dev = to_dev(case)
+        lengths = list(case.lengths)
+        if len(lengths) == 4:
+            lengths[1] = 0  # an empty request between split ones
+        indptr, idx, _ = pack_decode(dev, case.requests, lengths, case.local_capacity)
+        ref, ref_lse = OA.decode_from_indices(case.decode_q(), case.k_local, case.v_local, case.peer_k,
+                                              case.peer_v, indptr.cpu().tolist(), idx.cpu(), case.local_capacity)
+        runs.append((case, dev, indptr, idx, ref, ref_lse))
+    ws = torch.full((ops.decode_workspace_size(4, 300),), 0xA5, dtype=torch.uint8, device=DEV)
+    ops.decode_workspace_reset(ws, 4)
+    for rep in range(2):
+        for case, dev, indptr, idx, ref, ref_lse in runs:
+            for num_ctas in (1, 7, 148, 300):
+                B = len(case.lengths)
+                out = torch.full((B, 32, 128), float("nan"), dtype=torch.bfloat16, device=DEV)
+                lse = torch.full((B, 32), float("nan"), dtype=torch.float32, device=DEV)
+                ops.tiered_decode(case.decode_q().to(DEV), dev["k_local"], dev["v_local"], case.local_capacity,
+                                  dev["peer_k"], dev["peer_v"], indptr, idx, 128 ** -0.5, out, lse, ws, num_ctas)
+                torch.cuda.synchronize()
+                msg = f"{case.name} ctas={num_ctas} rep={rep}"
+                torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL, msg=msg)
+                torch.testing.assert_close(lse.cpu(), ref_lse, atol=ATOL, rtol=RTOL, msg=msg)
+                assert _status(ws) == 0
+                assert int(ws[256:256 + 4 * 8 * 4].view(torch.int32).abs().sum().item()) == 0, msg

@@ -73,7 +73,7 @@ def _with_workspace(q, k, v, pk, pv, indptr, idx, capacity, num_ctas):
     lse = torch.empty((q.shape[0], 32), dtype=torch.float32, device=DEV)
     nbytes = ops.decode_workspace_size(q.shape[0], num_ctas)
     ws = torch.full((nbytes // 4,), float("nan"), dtype=torch.float32, device=DEV).view(torch.uint8)
-    ws[:256] = 0  # the header (status word) starts cleared
+    ops.decode_workspace_reset(ws, q.shape[0])  # status word and arrival counters start cleared
     ops.tiered_decode(q, k, v, capacity, pk, pv, indptr, idx, 128 ** -0.5, out, lse, ws, num_ctas)
     return out, lse, ws
 
@@ -108,7 +108,8 @@ def test_noalloc_caller_status_word_and_size_limit():
     assert int(status.item()) == 0
     ref_out, _, _ = _with_workspace(*args, case.local_capacity, ops.default_ctas(0))
     torch.testing.assert_close(out.float(), ref_out.float(), atol=ATOL, rtol=RTOL)
-    # (num_ctas + batch) x 16896 B + 256 B must fit in the 8 MiB array: 148 CTAs + 400 requests do not.
+    # (num_ctas + batch) x 16896 B + the header and counters must fit in the 8 MiB array: 148 CTAs +
+    # 400 requests do not.
     rc, _, _ = _noalloc(*args, case.local_capacity, batch=400)
     assert rc == 3
     assert b"num_ctas + batch" in _lib.load().dual_last_error()
