@@ -78,9 +78,6 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-flashinfer", action="store_true",
                     help="config2: skip timing native FlashInfer FA2 on the same inputs after the dual_b200 arm")
-    ap.add_argument("--no-share", action="store_true",
-                    help="append workloads read in place: every work item reads its supplier rows itself "
-                         "(default: the items of a request and kv head share each fetched chunk)")
     ap.add_argument("--mig-ctas", type=int, default=64,
                     help="tiered workloads with migration: CTAs of the side-stream copy")
     ap.add_argument("--stage", choices=["range", "rows"], default=None,
@@ -1143,18 +1140,9 @@ def run_append(args):
         if stager is not None:
             stager.next(i)
 
-    # in place, the work items of a (request, kv head) share each chunk of supplier rows they fetch
-    # through local stage buffers shaped like the banks (the wrapper's default)
-    share = {}
-    if stager is None and not args.no_share:
-        share = dict(stage_k=[torch.empty_like(t, device=dev) for t in pk],
-                     stage_v=[torch.empty_like(t, device=dev) for t in pv],
-                     share_flags=torch.empty(ops.append_share_flags(kv), dtype=torch.int32, device=dev))
-
     def step(i):
         bk, bv = banks(i)
-        ops.tiered_append(q, k, v, C, bk, bv, qo_d, kv_d, full, True, 128 ** -0.5, work, out, lse, status,
-                          **share)
+        ops.tiered_append(q, k, v, C, bk, bv, qo_d, kv_d, full, True, 128 ** -0.5, work, out, lse, status)
         done(i)
 
     begin()
@@ -1182,8 +1170,7 @@ def run_append(args):
     # outputs and LSE back to pinned host memory, every step
     e2e = None
     from dual_b200.wrapper import BatchPrefillWithPagedKVCacheWrapper
-    wrapper = BatchPrefillWithPagedKVCacheWrapper(torch.empty(1 << 20, dtype=torch.uint8, device=dev), "NHD",
-                                                  share_remote_rows=not args.no_share)
+    wrapper = BatchPrefillWithPagedKVCacheWrapper(torch.empty(1 << 20, dtype=torch.uint8, device=dev), "NHD")
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(out.shape, dtype=torch.bfloat16).pin_memory()
     lse_host = torch.empty(lse.shape, dtype=torch.float32).pin_memory()
@@ -1250,10 +1237,7 @@ def run_append(args):
                                                              "overlapped with the previous layer's append",
                                                     "rows": "staged: LayerStager 'rows', the rows the index list "
                                                             "names copied by the row kernel before each append"}
-                                                   [args.stage] if stager is not None else
-                                                   ("read in place, each chunk fetched once per (request, kv "
-                                                    "head) and shared through local stage buffers" if share
-                                                    else "read in place by every work item")),
+                                                   [args.stage] if stager is not None else "read in place"),
                                  "l2": "K/V rows gathered from a pool larger than L2; no flush"},
                       "clocks": clk, "e2e": e2e, "cpu_baseline": cpu, "parity": parity,
                       "status": int(status.item()) | wrapper.status() | (stager.status() if stager else 0),

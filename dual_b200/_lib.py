@@ -58,10 +58,7 @@ SIGNATURES = {
         VP, VP, VP, C.c_int64, C.c_int, C.c_int,  # qo_indptr, kv_indptr, indices, num_indices, batch, causal
         C.c_double, VP, C.c_int64,             # sm_scale, work, num_work
         VP, C.c_int64, C.c_int64, VP,          # out, strides, lse
-        VP,                                    # status
-        C.POINTER(VP), C.POINTER(VP), C.c_int64, VP, C.c_int64,  # stage_k, stage_v, stride, flags, count
-        C.c_int, VP]),                         # device, stream
-    "dual_append_share_flags": (C.c_int, [VP, C.c_int, C.POINTER(C.c_int64)]),
+        VP, C.c_int, VP]),                     # status, device, stream
     "dual_pack_read_order": (C.c_int, [
         VP, VP, C.c_int64, C.c_int64, VP, VP, VP, VP, C.c_int, C.c_int64, C.c_int, C.c_int, VP, VP, VP, C.c_int, VP]),
     "dual_write_prefill_layout": (C.c_int, [

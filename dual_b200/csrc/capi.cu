@@ -181,22 +181,14 @@ int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_hos
   return DUAL_OK;
 }
 
-int dual_append_share_flags(const int32_t* kv_indptr_host, int batch, int64_t* count) {
-  g_last_error.clear();
-  if (batch < 0 || !count || (batch > 0 && !kv_indptr_host)) return fail(DUAL_EINVAL, "bad share flag arguments");
-  *count = dual::append_share_flags(kv_indptr_host, batch);
-  return DUAL_OK;
-}
-
 int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_local,
                        const void* v_local, int64_t local_stride_bytes, int64_t local_capacity,
                        const void* const* peer_k, const void* const* peer_v, int num_peers,
                        int64_t peer_stride_bytes, int64_t peer_slots, const int32_t* qo_indptr,
                        const int32_t* kv_indptr, const int32_t* unified_indices, int64_t num_indices, int batch,
                        int causal, double sm_scale, const int32_t* work, int64_t num_work, void* out,
-                       int64_t out_stride_token, int64_t out_stride_head, float* lse, uint32_t* status,
-                       void* const* stage_k, void* const* stage_v, int64_t stage_stride_bytes,
-                       uint32_t* share_flags, int64_t num_share_flags, int device, void* stream) {
+                       int64_t out_stride_token, int64_t out_stride_head, float* lse, uint32_t* status, int device,
+                       void* stream) {
   g_last_error.clear();
   if (batch < 0 || num_work < 0) return fail(DUAL_EINVAL, "negative batch or work count");
   if (batch == 0 || num_work == 0) return DUAL_OK;
@@ -220,15 +212,6 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
         return fail(DUAL_EINVAL, "peer bank %d pointer null or not 16-byte aligned", i);
   }
   if (!(sm_scale > 0.0)) return fail(DUAL_EINVAL, "sm_scale must be positive");
-  if (share_flags != nullptr) {
-    if (num_peers == 0 || !stage_k || !stage_v || num_share_flags <= 0)
-      return fail(DUAL_EINVAL, "remote-row sharing needs suppliers, one stage buffer pair per bank and flags");
-    if ((stage_stride_bytes & 15) || stage_stride_bytes < min_stride)
-      return fail(DUAL_EINVAL, "stage buffers need a 16-byte multiple slot stride >= 2048 B");
-    for (int i = 0; i < num_peers; ++i)
-      if (!stage_k[i] || !stage_v[i] || !aligned16(stage_k[i]) || !aligned16(stage_v[i]))
-        return fail(DUAL_EINVAL, "stage buffer %d pointer null or not 16-byte aligned", i);
-  }
   DUAL_USE_DEVICE(device);
   dual::AppendParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -260,19 +243,6 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.lse = lse;
   p.status = status;
   p.inject = g_inject.load(std::memory_order_relaxed);
-  if (share_flags != nullptr) {
-    for (int i = 0; i < dual::kMaxPeers; ++i) {
-      p.stage_k[i] = i < num_peers ? static_cast<const char*>(stage_k[i]) : nullptr;
-      p.stage_v[i] = i < num_peers ? static_cast<const char*>(stage_v[i]) : nullptr;
-    }
-    p.stage_stride = stage_stride_bytes;
-    p.share_flags = share_flags;
-    p.num_share_flags = num_share_flags;
-    // every chunk starts unclaimed in every launch
-    DUAL_CHECK_CUDA(cudaMemsetAsync(share_flags, 0, size_t(num_share_flags) * sizeof(uint32_t),
-                                    static_cast<cudaStream_t>(stream)),
-                    "share flag clear");
-  }
   cudaError_t e = dual::launch_tiered_append(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tiered append launch");
   return DUAL_OK;

@@ -69,11 +69,6 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: p stays <= 256 between
 // therefore round P like FlashInfer's FA2: the residual is neither stored nor multiplied (a third of
 // the tensor work on the 4-GPU append shapes).
 constexpr int64_t kResidualMaxEntries = 1024;
-// Remote-row sharing: chunks (64 list entries of one loader warp) with at least this many remote
-// entries are fetched once per (request, kv head) group; waiting for the fetcher gives up after
-// kShareWaitNs and reads the suppliers directly.
-constexpr unsigned kShareMinRemote = 8;
-constexpr unsigned long long kShareWaitNs = 2ull * 1000ull * 1000ull;
 
 constexpr int kQBytes = kRows * 256;       // 32 KB: [128 rows x 128 dims] bf16
 constexpr int kSlotBytes = kBN * 256;      // 32 KB: [128 entries x 128 dims] bf16
@@ -141,14 +136,11 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
   // indexing the kernel's parameter block instead would make every parameter a memory operand
   // that each asm statement with a memory clobber forces the compiler to reload
   __shared__ const char* s_peer[2][kMaxPeers];
-  __shared__ const char* s_stage[2][kMaxPeers];
   if (tid == 0) {
 #pragma unroll
     for (int i = 0; i < kMaxPeers; ++i) {  // constant indices: plain parameter loads
       s_peer[0][i] = p.peer_k[i];
       s_peer[1][i] = p.peer_v[i];
-      s_stage[0][i] = p.stage_k[i];
-      s_stage[1][i] = p.stage_v[i];
     }
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(slot_full + s, kLoadThreads);
@@ -241,9 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       }
     };
     const char *k0, *k1, *v0, *v1;  // row pointers of this lane's two entries, current tile
-    int32_t cur0 = page_of(0, 0), cur1 = page_of(0, 1);  // their page ids
-    resolve(cur0, k0, v0);
-    resolve(cur1, k1, v1);
+    resolve(page_of(0, 0), k0, v0);
+    resolve(page_of(0, 1), k1, v1);
     int32_t next0 = ntiles > 1 ? page_of(1, 0) : 0, next1 = ntiles > 1 ? page_of(1, 1) : 0;
     auto shfl_ptr = [](const char* ptr, int src_lane) {
       const unsigned long long v = reinterpret_cast<unsigned long long>(ptr);
@@ -251,120 +242,11 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       const uint32_t hi = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), src_lane);
       return reinterpret_cast<const char*>((static_cast<unsigned long long>(hi) << 32) | lo);
     };
-
-    // ---- remote-row sharing within a (request, kv head) group.  Every item of the group reads the
-    // same list, so its supplier rows would cross NVLink once per item (a peer's memory is not cached
-    // in this GPU's L2).  The group's longest query pair -- the fetcher, launched first of its group
-    // -- reads every 64-entry chunk with at least kShareMinRemote remote entries from the suppliers as
-    // usual and, once its copies of the chunk have landed, writes this kv head's slice of the chunk's
-    // remote rows into the stage buffers (laid out like the banks) and sets the chunk's flag.  The
-    // group's other items wait for the flag (only for chunks wholly inside their visible range) and
-    // read those rows from the stage buffers, i.e. from this GPU's L2 / HBM.  The fetcher never waits
-    // for another item, and a wait that runs out (kShareWaitNs) reads the suppliers instead, so
-    // sharing can neither deadlock nor change a result.
-    const int64_t pairs = (q_len + kPairTok - 1) / kPairTok;
-    bool share = p.share_flags != nullptr && pairs > 1;  // off for the rest of the item after a wait ran out
-    const bool fetcher = int64_t(pair) == pairs - 1;
-    const int64_t chunk_base = w.w;
-    auto remote_page = [&](int32_t id) { return np > 0 && static_cast<uint32_t>(id) > capacity; };
-    auto flag_of = [&](int jj) -> unsigned* {
-      const int64_t idx = (chunk_base + 2 * int64_t(jj) + lw) * kNumKvHeads + h;
-      return idx < p.num_share_flags ? p.share_flags + idx : nullptr;
-    };
-    // a chunk is shared when it lies wholly inside this item's visible range (then it does for the
-    // fetcher too, whose range is the group's longest) and holds enough remote rows
-    auto shared_chunk = [&](int jj, int32_t id0, int32_t id1) -> unsigned* {
-      if (!share || int64_t(jj) * kBN + 64 * lw + 64 > kv_end) return nullptr;
-      const unsigned nrem = __popc(__ballot_sync(0xffffffffu, remote_page(id0))) +
-                            __popc(__ballot_sync(0xffffffffu, remote_page(id1)));
-      return nrem >= kShareMinRemote ? flag_of(jj) : nullptr;
-    };
-    // stage row of a remote page id (nullptr for a local or bad one)
-    auto stage_row = [&](int32_t id, int plane) -> char* {
-      if (!remote_page(id)) return nullptr;
-      const uint32_t gid = static_cast<uint32_t>(id) - capacity - 1u;
-      const uint32_t bank = gid % np, phys = gid / np;
-      if (int64_t(phys) >= peer_slots) return nullptr;
-      return const_cast<char*>(s_stage[plane][bank]) + int64_t(phys) * p.stage_stride;
-    };
-    // fetcher: once its copies of tile jj have landed, write the chunk's remote rows (this kv head's
-    // 256 B of K and of V) to the stage buffers and publish the chunk; `block` = wait for the copies
-    // (else give up at once if they have not landed yet and return false)
-    auto publish = [&](int jj, int32_t id0, int32_t id1, bool block) -> bool {
-      const int u0 = 2 * jj;
-      if (!block) {
-        const bool landed = mbar_try_wait(slot_full + u0 % kSlots, uint32_t(u0 / kSlots) & 1u) &&
-                            mbar_try_wait(slot_full + (u0 + 1) % kSlots, uint32_t((u0 + 1) / kSlots) & 1u);
-        if (!__all_sync(0xffffffffu, landed)) return false;
-      }
-#pragma unroll 1
-      for (int plane = 0; plane < 2; ++plane) {
-        const int u = u0 + plane;
-        if (block && !wait(slot_full + u % kSlots, uint32_t(u / kSlots) & 1u)) return false;
-        const unsigned char* tile = smem + kOffSlot + (u % kSlots) * kSlotBytes;
-        char* const d0 = stage_row(id0, plane);
-        char* const d1 = stage_row(id1, plane);
-#pragma unroll 4
-        for (int i = 0; i < 32; ++i) {
-          const int rr = 2 * i + half;
-          char* dst = const_cast<char*>(shfl_ptr(i < 16 ? d0 : d1, rr & 31));
-          if (dst != nullptr) {
-            const uint4 v = *reinterpret_cast<const uint4*>(tile + tc::sw128_offset<kBN>(64 * lw + rr, chunk));
-            *reinterpret_cast<uint4*>(dst + off) = v;
-          }
-        }
-      }
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) atomicExch(flag_of(jj), 1u);
-      return true;
-    };
-    // fetcher's unpublished chunks at the top of iteration j: bit 0 = tile j-2 (its slots are refilled
-    // by this tile's V and the next tile's K, so it is published now, waiting if need be), bit 1 =
-    // tile j-1 (published now only if its copies have already landed); prev* hold their page ids
-    unsigned pending = 0;
-    int32_t prev0 = 0, prev1 = 0, prev20 = 0, prev21 = 0;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
       const int32_t after0 = j + 2 < ntiles ? page_of(j + 2, 0) : 0;  // lands while this tile issues
       const int32_t after1 = j + 2 < ntiles ? page_of(j + 2, 1) : 0;
       const int64_t tile0 = int64_t(j) * kBN;
-      if (pending & 1u) {
-        if (!publish(j - 2, prev20, prev21, true)) {
-          ok = false;
-          break;
-        }
-        pending &= ~1u;
-      }
-      if ((pending & 2u) && publish(j - 1, prev0, prev1, false)) pending &= ~2u;
-      unsigned* const fl = shared_chunk(j, cur0, cur1);
-      if (fl != nullptr) {
-        if (fetcher) {
-          pending |= 4u;
-        } else {
-          unsigned state = 0;
-          if (lane == 0) {
-            const unsigned long long t_start = globaltimer_ns();
-            do {
-              asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(state) : "l"(fl) : "memory");
-            } while (state == 0u && globaltimer_ns() - t_start < kShareWaitNs);
-          }
-          state = __shfl_sync(0xffffffffu, state, 0);
-          __syncwarp();  // every lane's reads of the stage buffers come after lane 0 saw the flag
-          if (state != 0u) {  // published: read this chunk's remote rows from the stage buffers
-            if (remote_page(cur0)) {
-              const char* sk = stage_row(cur0, 0);
-              if (sk != nullptr) { k0 = sk; v0 = stage_row(cur0, 1); }
-            }
-            if (remote_page(cur1)) {
-              const char* sk = stage_row(cur1, 0);
-              if (sk != nullptr) { k1 = sk; v1 = stage_row(cur1, 1); }
-            }
-          } else {
-            share = false;  // the fetcher is not getting there: read the suppliers from now on
-          }
-        }
-      }
 #pragma unroll 1
       for (int plane = 0; plane < 2; ++plane) {  // K then V of tile j
         const int u = 2 * j + plane, s = u % kSlots, f = u / kSlots;
@@ -387,13 +269,6 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         // (a test injection withholds the first K tile's arrival: the consumers' waits expire)
         if (!(u == 0 && (p.inject & DUAL_INJECT_APPEND_WITHHOLD_K0))) cp_async_mbar_arrive_noinc(slot_full + s);
       }
-      pending >>= 1;
-      prev20 = prev0;
-      prev21 = prev1;
-      prev0 = cur0;
-      prev1 = cur1;
-      cur0 = next0;
-      cur1 = next1;
       if (j + 1 < ntiles) {
         resolve(next0, k0, v0);
         resolve(next1, k1, v1);
@@ -401,9 +276,6 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       next0 = after0;
       next1 = after1;
     }
-    // the last tiles this item fetched for the group
-    if (ok && (pending & 1u)) ok = publish(ntiles - 2, prev20, prev21, true);
-    if (ok && (pending & 2u)) ok = publish(ntiles - 1, prev0, prev1, true);
     (void)ok;
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == kMmaWarp) {
@@ -673,33 +545,23 @@ int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, int batc
     for (int h = 0; h < kNumKvHeads; ++h) groups.push_back({cost, b, h});
   }
   std::stable_sort(groups.begin(), groups.end(), [](const Group& a, const Group& c) { return a.cost > c.cost; });
-  std::vector<int64_t> chunk_base(size_t(batch) + 1, 0);  // first 64-entry chunk of each request's list
-  for (int b = 0; b < batch; ++b) {
-    const int64_t L = int64_t(kv_indptr[b + 1]) - kv_indptr[b];
-    chunk_base[b + 1] = chunk_base[b] + 2 * ((std::max<int64_t>(L, 0) + kBN - 1) / kBN);
-  }
   int64_t n = 0;
   for (const Group& g : groups) {
     const int64_t q_len = int64_t(qo_indptr[g.b + 1]) - qo_indptr[g.b];
+    const int64_t L = int64_t(kv_indptr[g.b + 1]) - kv_indptr[g.b];
+    const int64_t prefix = L - q_len;
     const int64_t pairs = (q_len + kPairTok - 1) / kPairTok;
     for (int64_t t = pairs - 1; t >= 0; --t, ++n) {  // longest pair first
       if (work == nullptr || n >= max_work) continue;
+      const int64_t t_end = std::min(q_len, (t + 1) * kPairTok);
+      const int64_t kv_end = causal ? std::min(L, prefix + t_end) : L;
       work[4 * n + 0] = g.b;
       work[4 * n + 1] = g.h;
       work[4 * n + 2] = int32_t(t);
-      work[4 * n + 3] = int32_t(std::min<int64_t>(chunk_base[g.b], 0x7fffffff));
+      work[4 * n + 3] = int32_t(std::min<int64_t>((kv_end + kBN - 1) / kBN, 0x7fffffff));
     }
   }
   return n;
-}
-
-int64_t append_share_flags(const int32_t* kv_indptr, int batch) {
-  int64_t chunks = 0;
-  for (int b = 0; b < batch; ++b) {
-    const int64_t L = int64_t(kv_indptr[b + 1]) - kv_indptr[b];
-    chunks += 2 * ((std::max<int64_t>(L, 0) + kBN - 1) / kBN);
-  }
-  return chunks * kNumKvHeads;
 }
 
 cudaError_t launch_tiered_append(const AppendParams& p, cudaStream_t stream) {

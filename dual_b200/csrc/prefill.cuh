@@ -23,31 +23,20 @@ struct AppendParams {
   int batch;
   int causal;
   float scale_log2;
-  const int4* work;          // {request, kv head, query pair, first 64-entry chunk} from append_plan
+  const int4* work;          // {request, kv head, query tile, cost} from append_plan
   int num_work;
   __nv_bfloat16* out;        // [sum q, 32, 128]
   int64_t out_stride_tok, out_stride_head;
   float* lse;                // [sum q, 32] base 2, or nullptr
   unsigned* status;
   uint32_t inject;           // DUAL_INJECT_* bits (tests only; 0 in production)
-  // Remote-row sharing among the work items of one (request, kv head) (optional: share_flags null =
-  // every item reads its supplier rows itself).  stage_k/v[b]: local buffers laid out like bank b;
-  // one flag per (64-entry chunk of a request's list, kv head), zeroed before the launch.
-  const char* stage_k[kMaxPeers];
-  const char* stage_v[kMaxPeers];
-  int64_t stage_stride;
-  unsigned* share_flags;
-  int64_t num_share_flags;
 };
 
-// Host-side schedule: one item {request, kv head, 64-token query pair, index of the request's first
-// 64-entry list chunk} per pair, grouped by (request, kv head), groups longest first and pairs longest
-// first within a group.  Returns the number of items; writes min(n, max_work) items of 4 int32 into
-// `work` (may be null).
+// Host-side schedule: one item {request, kv head, 64-token query pair, kv tiles} per pair, grouped by
+// (request, kv head), groups longest first and pairs longest first within a group.
+// Returns the number of items; writes min(n, max_work) items of 4 int32 into `work` (may be null).
 int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, int batch, int causal, int32_t* work,
                     int64_t max_work);
-// Sharing flags a launch over these requests needs: 8 kv heads x sum over requests of 2 x ceil(L / 128).
-int64_t append_share_flags(const int32_t* kv_indptr, int batch);
 cudaError_t launch_tiered_append(const AppendParams& p, cudaStream_t stream);
 
 }  // namespace dual

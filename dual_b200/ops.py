@@ -113,8 +113,8 @@ def tiered_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
 
 
 def append_plan(qo_indptr, kv_indptr, causal: bool) -> torch.Tensor:
-    """Host-side work list (request, kv head, 64-token query pair, first 64-entry list chunk of the
-    request), grouped by (request, kv head), longest groups first, as an int32 CPU tensor [n, 4].
+    """Host-side work list (request, kv head, 64-token query pair, kv tiles it sees), grouped by
+    (request, kv head), longest groups first and pairs longest first, as an int32 CPU tensor [n, 4].
     ``qo_indptr`` / ``kv_indptr``: host sequences or CPU tensors."""
     qo = torch.as_tensor(qo_indptr, dtype=torch.int32).cpu().contiguous()
     kv = torch.as_tensor(kv_indptr, dtype=torch.int32).cpu().contiguous()
@@ -128,25 +128,11 @@ def append_plan(qo_indptr, kv_indptr, causal: bool) -> torch.Tensor:
     return work[: n.value]
 
 
-def append_share_flags(kv_indptr) -> int:
-    """32-bit sharing flags an append over these requests needs (``kv_indptr``: host sequence or CPU tensor)."""
-    kv = torch.as_tensor(kv_indptr, dtype=torch.int32).cpu().contiguous()
-    n = C.c_int64(0)
-    _lib.check(_lib.load().dual_append_share_flags(kv.data_ptr(), kv.numel() - 1, C.byref(n)))
-    return int(n.value)
-
-
 def tiered_append(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor, local_capacity: int,
                   peer_k: Sequence[torch.Tensor], peer_v: Sequence[torch.Tensor], qo_indptr: torch.Tensor,
                   kv_indptr: torch.Tensor, unified_indices: torch.Tensor, causal: bool, sm_scale: float,
-                  work: torch.Tensor, out: torch.Tensor, lse: Optional[torch.Tensor], status: torch.Tensor,
-                  stage_k: Optional[Sequence[torch.Tensor]] = None, stage_v: Optional[Sequence[torch.Tensor]] = None,
-                  share_flags: Optional[torch.Tensor] = None) -> None:
-    """Causal (or non-causal) append attention over the tiered pool; ``work`` from ``append_plan`` on the device.
-
-    With ``share_flags`` (``append_share_flags(kv_indptr)`` int32 words on the device) and one local
-    ``stage_k`` / ``stage_v`` buffer per supplier bank (the banks' shape), the work items of a request
-    and kv head fetch each chunk of supplier rows once and share it through the stage buffers."""
+                  work: torch.Tensor, out: torch.Tensor, lse: Optional[torch.Tensor], status: torch.Tensor) -> None:
+    """Causal (or non-causal) append attention over the tiered pool; ``work`` from ``append_plan`` on the device."""
     dev = _dev(q)
     _check(q.dtype == torch.bfloat16 and q.dim() == 3 and tuple(q.shape[1:]) == (NUM_QO_HEADS, HEAD_DIM)
            and q.stride(2) == 1, "q must be bf16 [sum q, 32, 128]")
@@ -163,28 +149,13 @@ def tiered_append(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
     pv = (C.c_void_p * max(n, 1))(*[t.data_ptr() for t in peer_v])
     ps = _pool_stride(peer_k[0], "peer_k0") if n else 0
     slots = peer_k[0].shape[0] if n else 0
-    sk = sv = None
-    ss, nflags = 0, 0
-    if share_flags is not None:
-        _check(stage_k is not None and stage_v is not None and len(stage_k) == n and len(stage_v) == n,
-               "sharing needs one stage_k / stage_v buffer per supplier bank")
-        ss = _pool_stride(stage_k[0], "stage_k0")
-        for i in range(n):
-            _check(stage_k[i].shape[0] >= slots and stage_v[i].shape[0] >= slots and stage_k[i].device == q.device
-                   and stage_v[i].device == q.device and _pool_stride(stage_k[i], "stage_k") == ss
-                   and _pool_stride(stage_v[i], "stage_v") == ss,
-                   "stage buffers: local, at least as many rows as the banks, one slot stride")
-        _check(share_flags.dtype in (torch.int32, torch.uint32) and share_flags.is_contiguous()
-               and share_flags.device == q.device, "share_flags must be contiguous 32-bit words on q's device")
-        sk, sv = _ptrs(stage_k), _ptrs(stage_v)
-        nflags = share_flags.numel()
     lib = _lib.load()
     _lib.check(lib.dual_tiered_append(
         q.data_ptr(), q.stride(0), q.stride(1), k_local.data_ptr(), v_local.data_ptr(), ls, int(local_capacity),
         pk, pv, n, ps, slots, qo_indptr.data_ptr(), kv_indptr.data_ptr(), unified_indices.data_ptr(),
         unified_indices.numel(), qo_indptr.numel() - 1, int(bool(causal)), float(sm_scale), work.data_ptr(),
-        work.shape[0], out.data_ptr(), out.stride(0), out.stride(1), _ptr(lse), status.data_ptr(),
-        sk, sv, ss, _ptr(share_flags), nflags, dev, _stream(q.device)))
+        work.shape[0], out.data_ptr(), out.stride(0), out.stride(1), _ptr(lse), status.data_ptr(), dev,
+        _stream(q.device)))
 
 
 def pack_read_order(tier: torch.Tensor, slot: torch.Tensor, req_pool_indices: torch.Tensor,

@@ -150,17 +150,12 @@ class BatchPrefillWithPagedKVCacheWrapper:
     def __init__(self, float_workspace_buffer: torch.Tensor, kv_layout: str = "NHD", use_cuda_graph: bool = False,
                  qo_indptr_buf=None, paged_kv_indptr_buf=None, paged_kv_indices_buf=None,
                  paged_kv_last_page_len_buf=None, custom_mask_buf=None, mask_indptr_buf=None,
-                 backend: str = "auto", jit_args=None, share_remote_rows: bool = True):
-        """``share_remote_rows``: the work items of a request and kv head fetch each chunk of supplier
-        rows over NVLink once and share it through local stage buffers the wrapper allocates (as many
-        rows as the banks, once), instead of every 64-token query pair reading it again."""
+                 backend: str = "auto", jit_args=None):
         if kv_layout != "NHD":
             raise ValueError("only the NHD layout is supported")
         self.device = float_workspace_buffer.device
         self._float_workspace = float_workspace_buffer
         self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self._share = bool(share_remote_rows)
-        self._stage = None
         self._plan = None
         self._custom_mask_buf = None
         self._window_left = -1
@@ -185,9 +180,7 @@ class BatchPrefillWithPagedKVCacheWrapper:
         qo_h = torch.as_tensor(qo_indptr).to("cpu", torch.int32)
         kv_h = torch.as_tensor(paged_kv_indptr).to("cpu", torch.int32)
         work = ops.append_plan(qo_h, kv_h, causal)
-        flags = (torch.empty(max(ops.append_share_flags(kv_h), 1), dtype=torch.int32, device=self.device)
-                 if self._share else None)
-        self._plan = dict(qo=qo_h.to(self.device, non_blocking=non_blocking), flags=flags,
+        self._plan = dict(qo=qo_h.to(self.device, non_blocking=non_blocking),
                           kv=kv_h.to(self.device, non_blocking=non_blocking),
                           indices=torch.as_tensor(paged_kv_indices).to(self.device, torch.int32),
                           work=work.to(self.device, non_blocking=non_blocking), causal=bool(causal),
@@ -211,23 +204,9 @@ class BatchPrefillWithPagedKVCacheWrapper:
             out = torch.empty_like(q)
         if return_lse and lse is None:
             lse = torch.empty((q.shape[0], ops.NUM_QO_HEADS), dtype=torch.float32, device=q.device)
-        share = {}
-        if peer_k and pl["flags"] is not None:
-            stage_k, stage_v = self._stage_buffers(peer_k)
-            share = dict(stage_k=stage_k, stage_v=stage_v, share_flags=pl["flags"])
         ops.tiered_append(q, k, v, capacity, peer_k, peer_v, pl["qo"], pl["kv"], indices, pl["causal"], scale,
-                          pl["work"], out, lse if return_lse else None, self._status, **share)
+                          pl["work"], out, lse if return_lse else None, self._status)
         return (out, lse) if return_lse else out
-
-    def _stage_buffers(self, banks):
-        """Local stage buffers for remote-row sharing, one K and one V buffer per supplier bank, shaped
-        like the banks; allocated on first use and reused by every layer with banks of that shape."""
-        key = (len(banks), tuple(banks[0].shape))
-        if self._stage is None or self._stage[0] != key:
-            mk = lambda: [torch.empty(tuple(banks[0].shape), dtype=torch.bfloat16, device=self.device)
-                          for _ in banks]
-            self._stage = (key, mk(), mk())
-        return self._stage[1], self._stage[2]
 
     run_return_lse = functools.partialmethod(run, return_lse=True)
 

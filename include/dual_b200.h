@@ -40,8 +40,7 @@ extern "C" {
 /* Thread-local message of the last failing call ("" if none). */
 const char* dual_last_error(void);
 /* ABI version of this library (major * 100 + minor): 200 = the merge inside the decode kernel (a
- * workspace with arrival counters, dual_decode_workspace_reset) and remote-row sharing arguments on
- * dual_tiered_append. */
+ * workspace with arrival counters, dual_decode_workspace_reset). */
 int dual_abi_version(void);
 
 /* ------------------------------------------------------- tiered decode ---
@@ -133,24 +132,14 @@ int dual_decode_noalloc_status(uint32_t* value_out, int device, void* stream);
  * causal != 0 query token i sees entry j iff j < L_b - q_b (history, any order) or
  * j - (L_b - q_b) <= i (the query suffix, in order -- the packer's Full list).
  * dual_append_plan (host): from HOST copies of qo_indptr / kv_indptr, writes the work list
- * (4 int32 per item: request, kv head, 64-token query pair, index of the request's first 64-entry
- * list chunk), grouped by (request, kv head) so a group's items run together and share K/V rows in
- * L2, groups longest first and pairs longest first within a group; returns the item count in
- * *num_work (call with work=NULL to size it).  The work list is then copied to
+ * (4 int32 per item: request, kv head, 64-token query pair, 128-entry kv tiles), grouped by
+ * (request, kv head) so a group's items run together and share K/V rows in L2, groups longest
+ * first and pairs longest first within a group; returns the item count in *num_work (call with
+ * work=NULL to size it).  The work list is then copied to
  * the device and passed to dual_tiered_append with the DEVICE indptrs.
- * q/out [sum q, 32, 128] bf16; lse [sum q, 32] fp32 base 2 or NULL; status: device word.
- * Remote-row sharing (optional; share_flags = NULL reads supplier rows in place per item): a
- * supplier row crosses NVLink once per work item that reads it, i.e. once per 64-token query pair
- * of its request (a peer's memory is not cached in the local L2).  With share_flags, the items of a
- * (request, kv head) fetch each 64-entry list chunk that holds remote rows once: the group's longest
- * query pair reads it from the suppliers and writes its remote rows into stage_k / stage_v[b] (local
- * buffers laid out like bank b, stage_stride_bytes per row, as many rows as peer_slots); the others
- * wait (bounded; afterwards they read the suppliers) and read them from there.  share_flags holds
- * num_share_flags = dual_append_share_flags(...) 32-bit words, zeroed by this call before the
- * kernel; results do not depend on the sharing. */
+ * q/out [sum q, 32, 128] bf16; lse [sum q, 32] fp32 base 2 or NULL; status: device word. */
 int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, int batch, int causal,
                      int32_t* work_host, int64_t max_work, int64_t* num_work);
-int dual_append_share_flags(const int32_t* kv_indptr_host, int batch, int64_t* count);
 int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                        const void* k_local, const void* v_local, int64_t local_stride_bytes,
                        int64_t local_capacity,
@@ -160,8 +149,7 @@ int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_h
                        const int32_t* unified_indices, int64_t num_indices, int batch, int causal,
                        double sm_scale, const int32_t* work, int64_t num_work,
                        void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
-                       uint32_t* status, void* const* stage_k, void* const* stage_v, int64_t stage_stride_bytes,
-                       uint32_t* share_flags, int64_t num_share_flags, int device, void* stream);
+                       uint32_t* status, int device, void* stream);
 
 /* ------------------------------------------------------ read-order packer ---
  * Replaces Triton _count_remote/_pack_indices + Engine.prepare (peer/backend.py:22-79)

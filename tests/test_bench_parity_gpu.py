@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 def _args(workload, **kw):
     return types.SimpleNamespace(workload=workload, seed=20261101, mig_ctas=64, warmup=1, steps=1, stage=None,
-                                 no_share=False, no_e2e=True, no_cpu_baseline=True, **kw)
+                                 no_e2e=True, no_cpu_baseline=True, **kw)
 
 
 def test_decode_sampler_on_small_workload():

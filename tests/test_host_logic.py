@@ -26,11 +26,11 @@ def test_append_plan_covers_every_item_once_grouped_longest_first(causal):
     items = [tuple(x) for x in w[:, :3]]
     expect = {(b, h, t) for b, q in enumerate(qlens) for h in range(8) for t in range((q + PAIR - 1) // PAIR)}
     assert len(items) == len(set(items)) and set(items) == expect
-    # fourth field: the first 64-entry chunk of the request's list (remote-row sharing flags)
-    chunk_base = np.concatenate([[0], np.cumsum([2 * ((L + TILE - 1) // TILE) for L in kvlens])])
-    for b, h, t, base in w:
-        assert base == chunk_base[b]
-    assert ops.append_share_flags(np.concatenate([[0], np.cumsum(kvlens)]).astype(np.int32)) == 8 * chunk_base[-1]
+    # costs: kv tiles the item's query pair can see
+    for b, h, t, cost in w:
+        q, L = qlens[b], kvlens[b]
+        end = min(L, L - q + min(q, (t + 1) * PAIR)) if causal else L
+        assert cost == (end + TILE - 1) // TILE
     # each (request, kv head) group is contiguous, groups by descending total length, pairs descending
     groups = [(b, h) for b, h, _, _ in w]
     change = [i for i in range(1, len(groups)) if groups[i] != groups[i - 1]]
