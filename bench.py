@@ -1036,7 +1036,9 @@ def append_setup(args, workload):
     ops.pack_read_order(tier, slot, req, seq, C, 5, 32, full, prefix_lens=pre)
     qo = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
     kv = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
-    work = ops.append_plan(qo, kv, True).to(dev)
+    # per-request remote counts (the tier manager's host mirror in a server) let the plan spread the
+    # mostly-remote requests' items over the launch
+    work = ops.append_plan(qo, kv, True, remote.astype(np.int32)).to(dev)
     Q = int(qlens.sum())
     q = torch.empty((Q, 32, 128), dtype=torch.bfloat16, device=dev).normal_(generator=g)
     out = torch.empty_like(q)
@@ -1181,7 +1183,7 @@ def run_append(args):
     def e2e_step(i):
         q_dev.copy_(q_host, non_blocking=True)
         wrapper.plan(qo_t, kv_t, full, torch.ones(B, dtype=torch.int32), 32, 8, 128, 1, causal=True,
-                     q_data_type=torch.bfloat16)
+                     q_data_type=torch.bfloat16, remote_counts=S.remote)
         tail = peers if stager is None else stager.tail(i)
         o_, l_ = wrapper.run_return_lse(q_dev, (k.unsqueeze(1), v.unsqueeze(1)), *tail, full, C, 128 ** -0.5)
         done(i)

@@ -49,7 +49,7 @@ SIGNATURES = {
         VP, C.c_int,                           # status (nullable), num_ctas
         C.c_int, VP]),                         # device, stream
     "dual_decode_noalloc_status": (C.c_int, [U32P, C.c_int, VP]),
-    "dual_append_plan": (C.c_int, [VP, VP, C.c_int, C.c_int, VP, C.c_int64, C.POINTER(C.c_int64)]),
+    "dual_append_plan": (C.c_int, [VP, VP, VP, C.c_int, C.c_int, VP, C.c_int64, C.POINTER(C.c_int64)]),
     "dual_tiered_append": (C.c_int, [
         VP, C.c_int64, C.c_int64,              # q, strides
         VP, VP, C.c_int64, C.c_int64,          # k_local, v_local, local stride, capacity

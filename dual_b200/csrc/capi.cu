@@ -166,8 +166,8 @@ int dual_decode_workspace_reset(void* workspace, size_t workspace_bytes, int bat
   return DUAL_OK;
 }
 
-int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, int batch, int causal,
-                     int32_t* work_host, int64_t max_work, int64_t* num_work) {
+int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, const int32_t* remote_counts_host,
+                     int batch, int causal, int32_t* work_host, int64_t max_work, int64_t* num_work) {
   g_last_error.clear();
   if (batch < 0 || !num_work) return fail(DUAL_EINVAL, "bad append plan arguments");
   if (batch > 0 && (!qo_indptr_host || !kv_indptr_host)) return fail(DUAL_EINVAL, "null indptr");
@@ -177,7 +177,10 @@ int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_hos
     if (ql < 0 || kl < 0) return fail(DUAL_EINVAL, "request %d: negative length", b);
     if (causal && kl < ql) return fail(DUAL_EINVAL, "request %d: causal append needs kv length >= query length", b);
   }
-  *num_work = dual::append_plan(qo_indptr_host, kv_indptr_host, batch, causal, work_host, max_work);
+  if (remote_counts_host)
+    for (int b = 0; b < batch; ++b)
+      if (remote_counts_host[b] < 0) return fail(DUAL_EINVAL, "request %d: negative remote count", b);
+  *num_work = dual::append_plan(qo_indptr_host, kv_indptr_host, remote_counts_host, batch, causal, work_host, max_work);
   return DUAL_OK;
 }
 

@@ -442,10 +442,12 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
             const uint64_t pp = f2_pack(p0, p1);
             rs2[i & 1] = f2_add(rs2[i & 1], pp);
             hi[i] = pack_bf16x2(p0, p1);
-            const uint64_t hh = f2_pack(__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xffff0000u));
-            float l0, l1;
-            f2_unpack(f2_sub(pp, hh), l0, l1);
-            lo[i] = pack_bf16x2(l0, l1);
+            if (use_lo) {  // the residual only where it is multiplied (1.7 % of a config-4 layer)
+              const uint64_t hh = f2_pack(__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xffff0000u));
+              float l0, l1;
+              f2_unpack(f2_sub(pp, hh), l0, l1);
+              lo[i] = pack_bf16x2(l0, l1);
+            }
           }
           tc::st8u(tS + col + 8 * sub, hi);
           if (use_lo) tc::st8u(tS + col + 16 + 8 * sub, lo);
@@ -530,11 +532,27 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
 // (ordering the items by cost alone interleaves groups, and on the 4-GPU append shapes every K/V
 // row was read from DRAM ~4.3 times); the pairs of a group differ in cost by at most
 // q / 128 tiles, so the order stays close to longest-processing-time-first.
-int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, int batch, int causal, int32_t* work,
-                    int64_t max_work) {
+//
+// With per-request remote counts, the items of requests whose list is mostly remote (share above
+// kSpreadRemoteShare) are spread evenly over the first kSpreadSpan of the launch order, longest
+// first, between the others.  A peer's rows are not cached in this GPU's L2, so every item of such a
+// request reads its rows over NVLink again; launched together (as the grouped order would), the
+// items of the ~95 %-remote requests of the 4-GPU append shapes saturate NVLink ingress while the
+// rest of the GPU waits (12.6 ms per layer with the banks on a peer), spread out they share it with
+// compute-bound items (9.26 ms, against 9.19 ms with the rows staged into local memory first).
+namespace {
+constexpr double kSpreadRemoteShare = 0.5;
+constexpr double kSpreadSpan = 0.9;
+}  // namespace
+
+int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* remote, int batch, int causal,
+                    int32_t* work, int64_t max_work) {
   struct Group {
     int64_t cost;
     int b, h;
+  };
+  struct Item {
+    int32_t b, h, t, tiles;
   };
   std::vector<Group> groups;
   for (int b = 0; b < batch; ++b) {
@@ -545,21 +563,36 @@ int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, int batc
     for (int h = 0; h < kNumKvHeads; ++h) groups.push_back({cost, b, h});
   }
   std::stable_sort(groups.begin(), groups.end(), [](const Group& a, const Group& c) { return a.cost > c.cost; });
-  int64_t n = 0;
+  auto heavy = [&](int b) {
+    const int64_t L = int64_t(kv_indptr[b + 1]) - kv_indptr[b];
+    return remote != nullptr && L > 0 && double(remote[b]) > kSpreadRemoteShare * double(L);
+  };
+  std::vector<Item> light, spread;
   for (const Group& g : groups) {
     const int64_t q_len = int64_t(qo_indptr[g.b + 1]) - qo_indptr[g.b];
     const int64_t L = int64_t(kv_indptr[g.b + 1]) - kv_indptr[g.b];
     const int64_t prefix = L - q_len;
     const int64_t pairs = (q_len + kPairTok - 1) / kPairTok;
-    for (int64_t t = pairs - 1; t >= 0; --t, ++n) {  // longest pair first
-      if (work == nullptr || n >= max_work) continue;
+    for (int64_t t = pairs - 1; t >= 0; --t) {  // longest pair first
       const int64_t t_end = std::min(q_len, (t + 1) * kPairTok);
       const int64_t kv_end = causal ? std::min(L, prefix + t_end) : L;
-      work[4 * n + 0] = g.b;
-      work[4 * n + 1] = g.h;
-      work[4 * n + 2] = int32_t(t);
-      work[4 * n + 3] = int32_t(std::min<int64_t>((kv_end + kBN - 1) / kBN, 0x7fffffff));
+      const Item it{g.b, g.h, int32_t(t), int32_t(std::min<int64_t>((kv_end + kBN - 1) / kBN, 0x7fffffff))};
+      (heavy(g.b) ? spread : light).push_back(it);
     }
+  }
+  std::stable_sort(spread.begin(), spread.end(), [](const Item& a, const Item& c) { return a.tiles > c.tiles; });
+  const int64_t n = int64_t(light.size() + spread.size());
+  if (work == nullptr) return n;
+  // merge: the k-th spread item goes at position floor(k * span * n / |spread|) or the first free one after
+  size_t li = 0, si = 0;
+  for (int64_t i = 0; i < n && i < max_work; ++i) {
+    bool take_spread = si < spread.size() &&
+                       (li >= light.size() || double(i) >= double(si) * kSpreadSpan * double(n) / double(spread.size()));
+    const Item& it = take_spread ? spread[si++] : light[li++];
+    work[4 * i + 0] = it.b;
+    work[4 * i + 1] = it.h;
+    work[4 * i + 2] = it.t;
+    work[4 * i + 3] = it.tiles;
   }
   return n;
 }

@@ -33,10 +33,11 @@ struct AppendParams {
 };
 
 // Host-side schedule: one item {request, kv head, 64-token query pair, kv tiles} per pair, grouped by
-// (request, kv head), groups longest first and pairs longest first within a group.
+// (request, kv head), groups longest first and pairs longest first within a group; with per-request
+// remote counts (`remote`, may be null), the items of mostly-remote requests spread over the launch.
 // Returns the number of items; writes min(n, max_work) items of 4 int32 into `work` (may be null).
-int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, int batch, int causal, int32_t* work,
-                    int64_t max_work);
+int64_t append_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* remote, int batch, int causal,
+                    int32_t* work, int64_t max_work);
 cudaError_t launch_tiered_append(const AppendParams& p, cudaStream_t stream);
 
 }  // namespace dual

@@ -112,19 +112,25 @@ def tiered_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
         dev, _stream(q.device)))
 
 
-def append_plan(qo_indptr, kv_indptr, causal: bool) -> torch.Tensor:
+def append_plan(qo_indptr, kv_indptr, causal: bool, remote_counts=None) -> torch.Tensor:
     """Host-side work list (request, kv head, 64-token query pair, kv tiles it sees), grouped by
     (request, kv head), longest groups first and pairs longest first, as an int32 CPU tensor [n, 4].
-    ``qo_indptr`` / ``kv_indptr``: host sequences or CPU tensors."""
+    ``qo_indptr`` / ``kv_indptr``: host sequences or CPU tensors.  ``remote_counts`` (optional, per
+    request: list entries on suppliers) spreads the items of mostly-remote requests over the launch."""
     qo = torch.as_tensor(qo_indptr, dtype=torch.int32).cpu().contiguous()
     kv = torch.as_tensor(kv_indptr, dtype=torch.int32).cpu().contiguous()
     B = qo.numel() - 1
+    rc = None
+    if remote_counts is not None:
+        rc = torch.as_tensor(remote_counts, dtype=torch.int32).cpu().contiguous()
+        _check(rc.numel() == B, "remote_counts needs one count per request")
     lib = _lib.load()
     n = C.c_int64(0)
-    _lib.check(lib.dual_append_plan(qo.data_ptr(), kv.data_ptr(), B, int(bool(causal)), None, 0, C.byref(n)))
-    work = torch.empty((max(n.value, 1), 4), dtype=torch.int32)
-    _lib.check(lib.dual_append_plan(qo.data_ptr(), kv.data_ptr(), B, int(bool(causal)), work.data_ptr(), n.value,
+    _lib.check(lib.dual_append_plan(qo.data_ptr(), kv.data_ptr(), _ptr(rc), B, int(bool(causal)), None, 0,
                                     C.byref(n)))
+    work = torch.empty((max(n.value, 1), 4), dtype=torch.int32)
+    _lib.check(lib.dual_append_plan(qo.data_ptr(), kv.data_ptr(), _ptr(rc), B, int(bool(causal)), work.data_ptr(),
+                                    n.value, C.byref(n)))
     return work[: n.value]
 
 

@@ -168,7 +168,10 @@ class BatchPrefillWithPagedKVCacheWrapper:
              custom_mask=None, packed_custom_mask=None, causal: bool = False, pos_encoding_mode: str = "NONE",
              use_fp16_qk_reduction: bool = False, sm_scale: Optional[float] = None, window_left: int = -1,
              logits_soft_cap: Optional[float] = None, rope_scale=None, rope_theta=None, q_data_type="bfloat16",
-             kv_data_type=None, non_blocking: bool = True, **kwargs) -> None:
+             kv_data_type=None, non_blocking: bool = True, remote_counts=None, **kwargs) -> None:
+        """FlashInfer's plan.  ``remote_counts`` (dual_b200 extension, optional): per request, how many
+        of its list entries are on suppliers (``TierManager.remote_counts``); mostly-remote requests'
+        work items are then spread over the launch so their NVLink reads overlap compute."""
         if (num_qo_heads, num_kv_heads, head_dim_qk, page_size) != (ops.NUM_QO_HEADS, ops.NUM_KV_HEADS,
                                                                     ops.HEAD_DIM, 1):
             raise ValueError("dual_b200 append is built for 32 q heads, 8 kv heads, head_dim 128, page_size 1")
@@ -179,7 +182,7 @@ class BatchPrefillWithPagedKVCacheWrapper:
             raise ValueError("only DefaultAttention (causal or not; no custom mask, window, soft cap, RoPE fusion)")
         qo_h = torch.as_tensor(qo_indptr).to("cpu", torch.int32)
         kv_h = torch.as_tensor(paged_kv_indptr).to("cpu", torch.int32)
-        work = ops.append_plan(qo_h, kv_h, causal)
+        work = ops.append_plan(qo_h, kv_h, causal, remote_counts)
         self._plan = dict(qo=qo_h.to(self.device, non_blocking=non_blocking),
                           kv=kv_h.to(self.device, non_blocking=non_blocking),
                           indices=torch.as_tensor(paged_kv_indices).to(self.device, torch.int32),

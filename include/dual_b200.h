@@ -135,11 +135,15 @@ int dual_decode_noalloc_status(uint32_t* value_out, int device, void* stream);
  * (4 int32 per item: request, kv head, 64-token query pair, 128-entry kv tiles), grouped by
  * (request, kv head) so a group's items run together and share K/V rows in L2, groups longest
  * first and pairs longest first within a group; returns the item count in *num_work (call with
- * work=NULL to size it).  The work list is then copied to
+ * work=NULL to size it).  remote_counts_host (NULL = unknown): per request, how many of its list
+ * entries are on suppliers; the items of requests that are more than half remote are then spread
+ * evenly over the first 90 % of the launch, longest first, so that their NVLink reads (a peer's rows
+ * are not cached in the local L2, so every query pair reads them again) overlap compute-bound items
+ * instead of saturating NVLink together.  The work list is then copied to
  * the device and passed to dual_tiered_append with the DEVICE indptrs.
  * q/out [sum q, 32, 128] bf16; lse [sum q, 32] fp32 base 2 or NULL; status: device word. */
-int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, int batch, int causal,
-                     int32_t* work_host, int64_t max_work, int64_t* num_work);
+int dual_append_plan(const int32_t* qo_indptr_host, const int32_t* kv_indptr_host, const int32_t* remote_counts_host,
+                     int batch, int causal, int32_t* work_host, int64_t max_work, int64_t* num_work);
 int dual_tiered_append(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                        const void* k_local, const void* v_local, int64_t local_stride_bytes,
                        int64_t local_capacity,

@@ -91,3 +91,31 @@ def test_prefill_plan_on_the_host_and_its_refusals():
                    args.pop("page_size"), causal=True, **args)
     with pytest.raises(ValueError):
         BatchPrefillWithPagedKVCacheWrapper(torch.empty(16, dtype=torch.uint8), "HND")
+
+
+def test_append_plan_spreads_mostly_remote_requests():
+    """With per-request remote counts, the items of requests more than half remote are spread evenly
+    over the first 90 % of the launch, longest first; every item still appears exactly once and the
+    others keep the grouped, longest-first order."""
+    rng = np.random.default_rng(9)
+    qlens = rng.integers(64, 700, 16).tolist()
+    kvlens = [q + int(rng.integers(1000, 8000)) for q in qlens]
+    remote = [int(0.95 * (L - q)) if b % 8 == 0 else int(0.03 * (L - q)) for b, (q, L) in
+              enumerate(zip(qlens, kvlens))]
+    qo = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    kv = np.concatenate([[0], np.cumsum(kvlens)]).astype(np.int32)
+    grouped = ops.append_plan(qo, kv, True).numpy()
+    spread = ops.append_plan(qo, kv, True, remote).numpy()
+    assert sorted(map(tuple, grouped)) == sorted(map(tuple, spread))
+    heavy = np.isin(spread[:, 0], [0, 8])
+    pos = np.nonzero(heavy)[0]
+    n, k = len(spread), len(pos)
+    assert k == int(np.isin(grouped[:, 0], [0, 8]).sum()) > 0
+    gaps = np.diff(pos)
+    assert pos[0] == 0 and pos[-1] < 0.9 * n + 2 and gaps.min() >= 1
+    assert gaps.max() - gaps.min() <= 1  # even spacing
+    assert list(spread[heavy][:, 3]) == sorted(spread[heavy][:, 3], reverse=True)
+    light = [tuple(x) for x in spread[~heavy]]
+    assert light == [tuple(x) for x in grouped if x[0] not in (0, 8)]
+    with pytest.raises(Exception):
+        ops.append_plan(qo, kv, True, [-1] * 16)
