@@ -65,35 +65,58 @@ struct Split {
 
 // Combine the partial states of request b for the 4 q heads of kv head h (one warp) and write the
 // bf16 output and the base-2 LSE.  CTAs glo..ghi cover the request; those with an empty range
-// wrote nothing.  Partials are read through L2 (other SMs wrote them during this launch).
+// wrote nothing.  Partials are read through L2 (other SMs wrote them during this launch).  The loads
+// of all four heads of a segment are independent and issued together, two segments at a time, so a
+// merge costs a few L2 round trips rather than one per value.
 __device__ __noinline__ void merge_request_heads(const TieredDecodeParams& p, const Split& sp, int b, int h,
-                                                    int glo, int ghi, int lane) {
+                                                 int glo, int ghi, int lane) {
   constexpr int64_t kSeg = int64_t(kNumQoHeads) * kPartialStride;
+  const float* base = p.partial + (int64_t(b) * kNumQoHeads + h * kGqa) * kPartialStride;
+  float M[kGqa];
+#pragma unroll
+  for (int r = 0; r < kGqa; ++r) M[r] = -INFINITY;
+#pragma unroll 4
+  for (int gg = glo; gg <= ghi; ++gg) {
+    if (!sp.nonempty(gg)) continue;
+#pragma unroll
+    for (int r = 0; r < kGqa; ++r) M[r] = fmaxf(M[r], __ldcg(base + gg * kSeg + r * kPartialStride + kHeadDim));
+  }
+  float D[kGqa];
+  float4 acc[kGqa];
+#pragma unroll
+  for (int r = 0; r < kGqa; ++r) {
+    D[r] = 0.f;
+    acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll 2
+  for (int gg = glo; gg <= ghi; ++gg) {
+    if (!sp.nonempty(gg)) continue;
+    float2 md[kGqa];
+    float4 v[kGqa];
+#pragma unroll
+    for (int r = 0; r < kGqa; ++r) {
+      const float* src = base + gg * kSeg + r * kPartialStride;
+      md[r] = __ldcg(reinterpret_cast<const float2*>(src + kHeadDim));
+      v[r] = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+    }
+#pragma unroll
+    for (int r = 0; r < kGqa; ++r) {
+      const float w = (md[r].x == -INFINITY) ? 0.f : exp2f(md[r].x - M[r]);
+      D[r] += w * md[r].y;
+      acc[r].x += w * v[r].x;
+      acc[r].y += w * v[r].y;
+      acc[r].z += w * v[r].z;
+      acc[r].w += w * v[r].w;
+    }
+  }
+#pragma unroll
   for (int r = 0; r < kGqa; ++r) {
     const int row = h * kGqa + r;
-    const float* base = p.partial + (int64_t(b) * kNumQoHeads + row) * kPartialStride;
-    float M = -INFINITY;
-    for (int gg = glo; gg <= ghi; ++gg)
-      if (sp.nonempty(gg)) M = fmaxf(M, __ldcg(base + gg * kSeg + kHeadDim));
-    float D = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int gg = glo; gg <= ghi; ++gg) {
-      if (!sp.nonempty(gg)) continue;
-      const float* src = base + gg * kSeg;
-      const float mm = __ldcg(src + kHeadDim);
-      const float w = (mm == -INFINITY) ? 0.f : exp2f(mm - M);
-      D += w * __ldcg(src + kHeadDim + 1);
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + lane);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
-    }
-    const float inv = 1.f / D;
+    const float inv = 1.f / D[r];
     __nv_bfloat16* orow = p.out + int64_t(b) * p.out_stride_tok + int64_t(row) * p.out_stride_head;
-    reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[0] = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-    reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[1] = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
-    if (p.lse != nullptr && lane == 0) p.lse[int64_t(b) * kNumQoHeads + row] = M + log2f(D);
+    reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[0] = __floats2bfloat162_rn(acc[r].x * inv, acc[r].y * inv);
+    reinterpret_cast<__nv_bfloat162*>(orow + lane * 4)[1] = __floats2bfloat162_rn(acc[r].z * inv, acc[r].w * inv);
+    if (p.lse != nullptr && lane == 0) p.lse[int64_t(b) * kNumQoHeads + row] = M[r] + log2f(D[r]);
   }
 }
 
@@ -224,6 +247,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __
   float m_run = -INFINITY, d_run = 0.f;
   int cur_b = -1;
   int n_seen = 0;
+  constexpr int kDeferredMerges = 4;
+  int deferred[kDeferredMerges];  // requests this warp merges once its range is done
+  int n_deferred = 0;
 
   auto load_q = [&](int b) {
     if (gi < kGqa) {
@@ -375,11 +401,25 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) tiered_decode_kernel(const __
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          __threadfence();
-          merge_request_heads(p, sp, cur_b, h, glo, ghi, lane);
+          // merge after this warp's range is done (a merge in mid-stream would hold up the CTA's
+          // pipeline); only when the short list is full is it done at once
+          if (n_deferred < kDeferredMerges) {
+            deferred[n_deferred++] = cur_b;
+          } else {
+            __threadfence();
+            merge_request_heads(p, sp, cur_b, h, glo, ghi, lane);
+          }
         }
       }
     }
+  }
+
+  // ---- the merges this warp deferred (it was the last of their CTAs to arrive)
+  if (n_deferred > 0) __threadfence();
+  for (int i = 0; i < n_deferred; ++i) {
+    int64_t start, end;
+    sp.range(p.indptr, deferred[i], start, end);
+    merge_request_heads(p, sp, deferred[i], h, sp.owner(start), sp.owner(end - 1), lane);
   }
 
   // ---- requests with no KV entries: output 0, LSE -inf, written by the CTA that owns their
