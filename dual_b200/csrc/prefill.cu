@@ -39,6 +39,7 @@
 // All waits are bounded; a timed-out wait records DUAL_STATUS_WAIT_TIMEOUT and every role
 // unwinds (no thread is left at a barrier the others skipped).
 #include <algorithm>
+#include <type_traits>
 #include <vector>
 
 #include "dual_b200.h"
@@ -57,8 +58,11 @@ constexpr int kBN = 128;                   // kv entries per kv tile
 constexpr int kSlots = 5;                  // ring slots, each one K or one V tile
 constexpr int kLoadWarps = 2;
 constexpr int kLoadThreads = kLoadWarps * 32;
+constexpr int kWarpEntries = kBN / kLoadWarps;  // kv entries of a tile each loader warp gathers
+constexpr int kLaneEntries = kWarpEntries / 32;  // entries whose row pointers one lane resolves
+static_assert(kLaneEntries == 1 || kLaneEntries == 2, "loader warps gather 32 or 64 entries of a tile");
 constexpr int kSoftmaxWarps = 4 * kQTiles;
-constexpr int kMmaWarp = kSoftmaxWarps + kLoadWarps;  // warp 10
+constexpr int kMmaWarp = kSoftmaxWarps + kLoadWarps;  // the last warp
 constexpr int kThreads = (kMmaWarp + 1) * 32;          // 352
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: p stays <= 256 between rescales
 // P enters P @ V as a bf16 high part plus its bf16 residual only in work items whose shortest query
@@ -191,8 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     cp_async_wait<0>();
     fence_proxy_async_smem();
     mbar_arrive(q_full);
-    // kv tiles: loader warp lw owns entries [64 lw, 64 lw + 64) of each tile.  Lane l resolves the
-    // page ids of entries 64 lw + l and 64 lw + 32 + l into K and V row pointers one tile ahead of
+    // kv tiles: loader warp lw owns entries [E lw, E lw + E) of each tile (E = kWarpEntries).  Lane l
+    // resolves the page ids of entries E lw + 32 e + l into K and V row pointers one tile ahead of
     // use (the ids themselves are loaded two tiles ahead); the copy loop then only shuffles a
     // pointer: 16 lanes cover one entry's 256 B (two full 128 B lines), so each warp-wide cp.async
     // moves two entries, coalesced.  Resolving inside the copy loop (the remote branch with its
@@ -207,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     const uint32_t np = static_cast<uint32_t>(max(p.num_peers, 0));
     unsigned* const status = p.status;
     const int64_t off = h * 256 + chunk * 16;
-    auto page_of = [&](int jj, int sub) -> int32_t {  // page id of entry 64 lw + 32 sub + lane (0 past the end)
-      const int64_t pos = int64_t(jj) * kBN + 64 * lw + 32 * sub + lane;
+    auto page_of = [&](int jj, int sub) -> int32_t {  // page id of entry E lw + 32 sub + lane (0 past the end)
+      const int64_t pos = int64_t(jj) * kBN + kWarpEntries * lw + 32 * sub + lane;
       return pos < kv_end ? __ldg(indices + pos) : 0;
     };
     // page id -> row pointers of both planes (page 0 of the local pool for a bad remote id, which is
@@ -232,10 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         }
       }
     };
-    const char *k0, *k1, *v0, *v1;  // row pointers of this lane's two entries, current tile
-    resolve(page_of(0, 0), k0, v0);
-    resolve(page_of(0, 1), k1, v1);
-    int32_t next0 = ntiles > 1 ? page_of(1, 0) : 0, next1 = ntiles > 1 ? page_of(1, 1) : 0;
+    const char *kr[kLaneEntries], *vr[kLaneEntries];  // row pointers of this lane's entries, current tile
+    int32_t next[kLaneEntries];
+#pragma unroll
+    for (int e = 0; e < kLaneEntries; ++e) {
+      resolve(page_of(0, e), kr[e], vr[e]);
+      next[e] = ntiles > 1 ? page_of(1, e) : 0;
+    }
     auto shfl_ptr = [](const char* ptr, int src_lane) {
       const unsigned long long v = reinterpret_cast<unsigned long long>(ptr);
       const uint32_t lo = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v), src_lane);
@@ -244,8 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     };
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
-      const int32_t after0 = j + 2 < ntiles ? page_of(j + 2, 0) : 0;  // lands while this tile issues
-      const int32_t after1 = j + 2 < ntiles ? page_of(j + 2, 1) : 0;
+      int32_t after[kLaneEntries];  // lands while this tile issues
+#pragma unroll
+      for (int e = 0; e < kLaneEntries; ++e) after[e] = j + 2 < ntiles ? page_of(j + 2, e) : 0;
       const int64_t tile0 = int64_t(j) * kBN;
 #pragma unroll 1
       for (int plane = 0; plane < 2; ++plane) {  // K then V of tile j
@@ -254,14 +262,13 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           ok = false;
           break;
         }
-        const char* const r0 = plane == 0 ? k0 : v0;
-        const char* const r1 = plane == 0 ? k1 : v1;
         unsigned char* dst_tile = smem + kOffSlot + s * kSlotBytes;
 #pragma unroll 8
-        for (int i = 0; i < 32; ++i) {
-          const int rr = 2 * i + half;  // entry within this warp's 64
-          const int row = 64 * lw + rr;
-          const char* src = shfl_ptr(i < 16 ? r0 : r1, rr & 31);
+        for (int i = 0; i < kWarpEntries / 2; ++i) {
+          const int rr = 2 * i + half;  // entry within this warp's share
+          const int row = kWarpEntries * lw + rr;
+          const char* const* rows = plane == 0 ? kr : vr;
+          const char* src = shfl_ptr(kLaneEntries == 1 || i < 16 ? rows[0] : rows[kLaneEntries - 1], rr & 31);
           const bool valid = tile0 + row < kv_end;
           cp_async_16_zfill(dst_tile + tc::sw128_offset<kBN>(row, chunk), src + off, valid);
         }
@@ -269,12 +276,11 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         // (a test injection withholds the first K tile's arrival: the consumers' waits expire)
         if (!(u == 0 && (p.inject & DUAL_INJECT_APPEND_WITHHOLD_K0))) cp_async_mbar_arrive_noinc(slot_full + s);
       }
-      if (j + 1 < ntiles) {
-        resolve(next0, k0, v0);
-        resolve(next1, k1, v1);
+#pragma unroll
+      for (int e = 0; e < kLaneEntries; ++e) {
+        if (j + 1 < ntiles) resolve(next[e], kr[e], vr[e]);
+        next[e] = after[e];
       }
-      next0 = after0;
-      next1 = after1;
     }
     (void)ok;
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -430,7 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       // P of 32 entries written over their own S columns: [0,16) hi pairs, [16,32) lo pairs.
       // hi = rn_bf16(p), lo = rn_bf16(p - hi), with the scale, the sums and the residual on packed
       // f32x2 arithmetic.
-      auto emit = [&](const float* xc, int col) {
+      auto emit_p = [&](const float* xc, int col, auto lo_tag) {
+        constexpr bool kLo = decltype(lo_tag)::value;
 #pragma unroll
         for (int sub = 0; sub < 2; ++sub) {  // 16 entries: 8 hi words, 8 lo words
           uint32_t hi[8], lo[8];
@@ -442,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
             const uint64_t pp = f2_pack(p0, p1);
             rs2[i & 1] = f2_add(rs2[i & 1], pp);
             hi[i] = pack_bf16x2(p0, p1);
-            if (use_lo) {  // the residual only where it is multiplied (1.7 % of a config-4 layer)
+            if (kLo) {  // the residual only where it is multiplied (1.7 % of a config-4 layer)
               const uint64_t hh = f2_pack(__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xffff0000u));
               float l0, l1;
               f2_unpack(f2_sub(pp, hh), l0, l1);
@@ -450,8 +457,14 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
             }
           }
           tc::st8u(tS + col + 8 * sub, hi);
-          if (use_lo) tc::st8u(tS + col + 16 + 8 * sub, lo);
+          if (kLo) tc::st8u(tS + col + 16 + 8 * sub, lo);
         }
+      };
+      auto emit = [&](const float* xc, int col) {
+        if (use_lo)
+          emit_p(xc, col, std::true_type{});
+        else
+          emit_p(xc, col, std::false_type{});
       };
       auto mask32 = [&](float* xc, int col) {
         if (needs_mask) {
