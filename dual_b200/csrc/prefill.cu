@@ -21,12 +21,13 @@
 //   * two query tiles of 32 tokens x 4 GQA heads = 2 x 128 MMA rows share every K/V tile;
 //     kv tiles are 128 entries: a tcgen05.mma of K = 16 costs the same ~76 cycles for any
 //     N <= 128, so N = 128 score tiles halve the QK^T instructions per key against N = 64;
-//   * loader warps (2) gather K and V tiles (128 entries x 256 B of this kv head, local HBM or
+//   * loader warps (4, one per SM sub-partition; with 2 the gathers paced the kernel) gather K and
+//     V tiles (128 entries x 256 B of this kv head, local HBM or
 //     a supplier's HBM through peer loads) with 16-byte cp.async, 16 lanes per entry so every
 //     warp instruction moves whole cache lines, into a 5-slot ring of 32 KB 128B-swizzled
 //     tiles filled in the order K0 V0 K1 V1 ...; each loader arrives on the slot's barrier when
 //     its copies land (cp.async.mbarrier.arrive), so loads run ahead of the tensor core;
-//   * one MMA thread issues, per kv tile j and query tile q: O_q += P_q(j-1) V(j-1) (hi and lo,
+//   * one MMA warp (one elected lane) issues, per kv tile j and query tile q: O_q += P_q(j-1) V(j-1) (hi and lo,
 //     A operand read from tensor memory) and then S_q = Q_q K(j)^T into the same TMEM columns
 //     (tcgen05.mma instructions of one thread execute in issue order, so the PV reads P before
 //     the next QK overwrites it); one commit per query tile and kv tile tells the softmax both
@@ -56,14 +57,14 @@ constexpr int kQTiles = 2;                 // query tiles per CTA
 constexpr int kPairTok = kQTok * kQTiles;  // 64 query tokens per work item
 constexpr int kBN = 128;                   // kv entries per kv tile
 constexpr int kSlots = 5;                  // ring slots, each one K or one V tile
-constexpr int kLoadWarps = 2;
+constexpr int kLoadWarps = 4;
 constexpr int kLoadThreads = kLoadWarps * 32;
 constexpr int kWarpEntries = kBN / kLoadWarps;  // kv entries of a tile each loader warp gathers
 constexpr int kLaneEntries = kWarpEntries / 32;  // entries whose row pointers one lane resolves
 static_assert(kLaneEntries == 1 || kLaneEntries == 2, "loader warps gather 32 or 64 entries of a tile");
 constexpr int kSoftmaxWarps = 4 * kQTiles;
 constexpr int kMmaWarp = kSoftmaxWarps + kLoadWarps;  // the last warp
-constexpr int kThreads = (kMmaWarp + 1) * 32;          // 352
+constexpr int kThreads = (kMmaWarp + 1) * 32;          // 416
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: p stays <= 256 between rescales
 // P enters P @ V as a bf16 high part plus its bf16 residual only in work items whose shortest query
 // row sees fewer than this many kv entries.  Rounding P to bf16 costs up to 2^-9 of each term; on
@@ -179,8 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
 
   if (warp >= kSoftmaxWarps && warp < kMmaWarp) {
     // ================================================================ loaders
-    const int lt = tid - kSoftmaxWarps * 32;  // 0..63
-    // query tiles: 256 rows x 16 chunks of 16 B, 64 threads
+    const int lt = tid - kSoftmaxWarps * 32;  // 0 .. kLoadThreads - 1
+    // query tiles: 256 rows x 16 chunks of 16 B over the loader threads
     for (int i = lt; i < kQTiles * kRows; i += kLoadThreads) {
       const int q = i / kRows, r = i % kRows;
       const int64_t tok = t_begin + q * kQTok + r / kGqa;
@@ -285,16 +286,23 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
     (void)ok;
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == kMmaWarp) {
-    // ================================================================ MMA issue (one thread)
+    // ================================================================ MMA issue (one warp, one lane)
     // Query tiles alternate (PV_0 QK_0, PV_1 QK_1), so the tensor core works on one tile while the
     // other is in softmax; within a tile PV_q(j-1) is issued before QK_q(j), which overwrites P_q.
-    if (lane == 0) {
+    // The whole warp runs the loop in warp-uniform control flow (every wait is a warp vote), so the
+    // descriptors and TMEM addresses are uniform values, and one elected lane issues each tcgen05
+    // instruction.  Run by lane 0 alone inside a divergent branch, the same loop cost the issuing
+    // thread ~100 cycles per MMA (traced with clock64 on config-4 shapes: 4 MMAs to an idle tensor
+    // core took 400 cycles), and that issue rate, not the tensor core, set the kernel's pace.
+    const bool leader = tc::elect_one();
+    auto wait_warp = [&](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, wait(bar, parity)); };
+    {
       constexpr uint32_t kIdescQK = tc::idesc_bf16_f32(128, kBN, 0, 0);
       constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, 0, 1);
       const uint32_t q_base = smem_addr(smem + kOffQ);
       const uint32_t slot_base = smem_addr(smem + kOffSlot);
       auto slot_addr = [&](int u) { return slot_base + uint32_t(u % kSlots) * kSlotBytes; };
-      auto slot_wait = [&](int u) { return wait(slot_full + u % kSlots, uint32_t(u / kSlots) & 1u); };
+      auto slot_wait = [&](int u) { return wait_warp(slot_full + u % kSlots, uint32_t(u / kSlots) & 1u); };
       // O_q (+)= P_q V(jj), k-steps of 16 entries, each a hi and a lo MMA with A from TMEM; part 0 is
       // entries 64..127 (k-steps 4..7, the first P the softmax writes), part 1 entries 0..63
       auto issue_pv_part = [&](int q, int jj, int part) {
@@ -306,20 +314,22 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           const int kb = part == 0 ? 4 + k : k;
           const uint64_t vdesc = tc::smem_desc_sw128(v_base + kb * 2048, kBN * 128, 1024);
           const uint32_t ph = tP + 32 * (kb >> 1) + 8 * (kb & 1);
-          tc::mma_bf16_ts(tO, ph, vdesc, kIdescPV, (jj > 0 || part > 0 || k > 0) ? 1u : 0u);
-          if (use_lo) tc::mma_bf16_ts(tO, ph + 16, vdesc, kIdescPV, 1u);
+          if (leader) {
+            tc::mma_bf16_ts(tO, ph, vdesc, kIdescPV, (jj > 0 || part > 0 || k > 0) ? 1u : 0u);
+            if (use_lo) tc::mma_bf16_ts(tO, ph + 16, vdesc, kIdescPV, 1u);
+          }
         }
       };
       // both parts of PV_q(jj), each once the softmax has written that part of P
       auto issue_pv = [&](int q, int jj) -> bool {
         for (int part = 0; part < 2; ++part) {
-          if (!wait(p_part + 2 * q + part, uint32_t(jj) & 1u)) return false;
+          if (!wait_warp(p_part + 2 * q + part, uint32_t(jj) & 1u)) return false;
           tc::fence_after_sync();
           issue_pv_part(q, jj, part);
         }
         return true;
       };
-      bool ok = wait(q_full, 0);
+      bool ok = wait_warp(q_full, 0);
       for (int j = 0; j < ntiles && ok; ++j) {
         const uint32_t k_base = slot_addr(2 * j);
         // K(j) landed, and with it V(j-1): each loader thread issues V(j-1) before K(j) and arrives
@@ -340,14 +350,17 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
           for (int kb = 0; kb < 8; ++kb) {
             const uint32_t off_q = (kb >> 2) * (kRows * 128) + (kb & 3) * 32;
             const uint32_t off_k = (kb >> 2) * (kBN * 128) + (kb & 3) * 32;
-            tc::mma_bf16(tmem + q * kBN, tc::smem_desc_sw128(qb + off_q, 16, 1024),
-                         tc::smem_desc_sw128(k_base + off_k, 16, 1024), kIdescQK, kb > 0);
+            if (leader)
+              tc::mma_bf16(tmem + q * kBN, tc::smem_desc_sw128(qb + off_q, 16, 1024),
+                           tc::smem_desc_sw128(k_base + off_k, 16, 1024), kIdescQK, kb > 0);
           }
-          tc::commit(s_full + q);  // S_q(j) written, PV_q(j-1) done
+          if (leader) tc::commit(s_full + q);  // S_q(j) written, PV_q(j-1) done
         }
         if (!ok) break;
-        tc::commit(slot_empty + (2 * j) % kSlots);                 // K(j) consumed by both QKs
-        if (j > 0) tc::commit(slot_empty + (2 * j - 1) % kSlots);  // V(j-1) consumed by both PVs
+        if (leader) {
+          tc::commit(slot_empty + (2 * j) % kSlots);                 // K(j) consumed by both QKs
+          if (j > 0) tc::commit(slot_empty + (2 * j - 1) % kSlots);  // V(j-1) consumed by both PVs
+        }
       }
       if (ok && ntiles > 0) {
         ok = slot_wait(2 * ntiles - 1);
@@ -355,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       }
       for (int q = 0; q < kQTiles && ok && ntiles > 0; ++q) {
         if (!issue_pv(q, ntiles - 1)) break;
-        tc::commit(o_done + q);
+        if (leader) tc::commit(o_done + q);
       }
     }
   } else {

@@ -37,6 +37,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, in
          (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 
+// One lane of a fully active warp (the same lane every time: the lowest), chosen by elect.sync.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t.reg .b32 l;\n\t"
+      "elect.sync l|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   const uint32_t z = 0;
   asm volatile(
