@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
   uint64_t* slot_full = bars;                    // [kSlots] count kLoadThreads
   uint64_t* slot_empty = bars + kSlots;          // [kSlots] count 1 (tcgen05.commit)
   uint64_t* s_full = bars + 2 * kSlots;          // [2]      count 1 (tcgen05.commit)
-  uint64_t* p_part = s_full + kQTiles;           // [2 x 2]  count 128: P of entries 64..127, then 0..63
+  uint64_t* p_part = s_full + kQTiles;           // [2 x 2]  count 128: P of entries 32..127, then 0..31
   uint64_t* o_done = p_part + 2 * kQTiles;       // [2]      count 1 (tcgen05.commit, last PV)
   uint64_t* q_full = o_done + kQTiles;           // [1]      count kLoadThreads
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars);
@@ -304,14 +304,16 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
       auto slot_addr = [&](int u) { return slot_base + uint32_t(u % kSlots) * kSlotBytes; };
       auto slot_wait = [&](int u) { return wait_warp(slot_full + u % kSlots, uint32_t(u / kSlots) & 1u); };
       // O_q (+)= P_q V(jj), k-steps of 16 entries, each a hi and a lo MMA with A from TMEM; part 0 is
-      // entries 64..127 (k-steps 4..7, the first P the softmax writes), part 1 entries 0..63
+      // entries 32..127 (k-steps 2..7, the first P the softmax writes), part 1 entries 0..31: the
+      // smaller the last part, the fewer MMAs stand between the end of a softmax and the next QK
+      // (96/32 against 64/64: 7.70-7.76 vs 7.81-7.84 ms on config 4, same box)
       auto issue_pv_part = [&](int q, int jj, int part) {
         const uint32_t v_base = slot_addr(2 * jj + 1);
         const uint32_t tP = tmem + q * kBN;
         const uint32_t tO = tmem + kColO + q * 128;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int kb = part == 0 ? 4 + k : k;
+        for (int k = 0; k < (part == 0 ? 6 : 2); ++k) {
+          const int kb = part == 0 ? 2 + k : k;
           const uint64_t vdesc = tc::smem_desc_sw128(v_base + kb * 2048, kBN * 128, 1024);
           const uint32_t ph = tP + 32 * (kb >> 1) + 8 * (kb & 1);
           if (leader) {
@@ -489,20 +491,20 @@ __global__ void __launch_bounds__(kThreads, 1) tiered_append_kernel(const __grid
         }
       };
       // x holds entries 64..127; entries 0..63 are read again into each half of x once it is
-      // consumed, overlapping the exponentials and the hand-off.  Each half of P goes to the MMA
-      // thread as soon as it is in tensor memory (with any rescaled O before it).
+      // consumed, overlapping the exponentials.  P of entries 32..127 goes to the MMA warp as soon
+      // as it is in tensor memory (with any rescaled O before it), then P of entries 0..31.
       emit(x, 64);
       tc::ld32(tS, x);
       emit(x + 32, 96);
+      tc::ld32(tS + 32, x + 32);
+      tc::wait_ld();
+      mask32(x + 32, 32);
+      emit(x + 32, 32);
       tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(p_part + 2 * q);
-      tc::ld32(tS + 32, x + 32);
-      tc::wait_ld();
       mask32(x, 0);
-      mask32(x + 32, 32);
       emit(x, 0);
-      emit(x + 32, 32);
       float r0, r1, r2, r3;
       f2_unpack(f2_add(rs2[0], rs2[1]), r0, r1);
       f2_unpack(f2_add(rs2[2], rs2[3]), r2, r3);
