@@ -21,14 +21,15 @@
 //   * two query tiles of 32 tokens x 4 GQA heads = 2 x 128 MMA rows share every K/V tile;
 //     kv tiles are 128 entries: a tcgen05.mma of K = 16 costs the same ~76 cycles for any
 //     N <= 128, so N = 128 score tiles halve the QK^T instructions per key against N = 64;
-//   * loader warps (4, one per SM sub-partition; with 2 the gathers paced the kernel) gather K and
-//     V tiles (128 entries x 256 B of this kv head, local HBM or
-//     a supplier's HBM through peer loads) with 16-byte cp.async, 16 lanes per entry so every
-//     warp instruction moves whole cache lines, into a 5-slot ring of 32 KB 128B-swizzled
-//     tiles filled in the order K0 V0 K1 V1 ...; each loader arrives on the slot's barrier when
-//     its copies land (cp.async.mbarrier.arrive), so loads run ahead of the tensor core;
-//   * one MMA warp (one elected lane) issues, per kv tile j and query tile q: O_q += P_q(j-1) V(j-1) (hi and lo,
-//     A operand read from tensor memory) and then S_q = Q_q K(j)^T into the same TMEM columns
+//   * loader warps (4, one per SM sub-partition; with 2 the gathers paced the kernel) gather K
+//     and V tiles (128 entries x 256 B of this kv head, local HBM or a supplier's HBM through
+//     peer loads) with 16-byte cp.async, 16 lanes per entry so every warp instruction moves
+//     whole cache lines, into a 5-slot ring of 32 KB 128B-swizzled tiles filled in the order
+//     K0 V0 K1 V1 ...; each loader arrives on the slot's barrier when its copies land
+//     (cp.async.mbarrier.arrive), so loads run ahead of the tensor core;
+//   * one MMA warp (one elected lane) issues, per kv tile j and query tile q:
+//     O_q += P_q(j-1) V(j-1) (hi, and lo where the residual is on; A operand read from tensor
+//     memory) and then S_q = Q_q K(j)^T into the same TMEM columns
 //     (tcgen05.mma instructions of one thread execute in issue order, so the PV reads P before
 //     the next QK overwrites it); one commit per query tile and kv tile tells the softmax both
 //     that S_q(j) is ready and that O_q is quiescent;
