@@ -18,8 +18,10 @@ under torchrun N/2 such pairs); config4, append-small, append-mid (causal append
 stages the supplier rows per layer); migration; fi-<workload> times native FlashInfer FA2 on the
 same inputs (the number to beat).
 
-Under torchrun (N > 1) every rank serves its own independent batch (decode
-shards by request; no collective on the data path): scaling "weak".
+Under torchrun (N > 1) the default is config 5's layout: N/2 (compute GPU r, supplier GPU r + N/2)
+pairs, each compute GPU decoding its own batch with its supplier's rows read over NVLink and a
+concurrent migration; `--workload config2` runs N independent all-local replicas instead.  Decode
+shards by request, with no collective on the data path: scaling "weak".
 ``--impl reference`` times the reference's CPU attention math (the fp32 oracle
 restatement of check_attention_output) on the host cores instead.
 """
